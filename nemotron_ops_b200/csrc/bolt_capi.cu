@@ -1,0 +1,328 @@
+// C ABI of libbolt_b200.so (declared in include/bolt_b200.h).
+//
+// Each bolt_* function is the host body of one reference op (the *State::ComputeV2 functions
+// of src/bolt_ops.cu): the same shape checks with the same messages, the same dispatch by
+// row count / K / iq2 mode, then the B200 kernels.  Exceptions never cross the ABI: every
+// failure becomes a status code plus a thread-local message.
+#include <cuda_runtime.h>
+
+#include <atomic>
+#include <initializer_list>
+#include <cstdlib>
+#include <mutex>
+#include <stdexcept>
+#include <string>
+
+#include "../../include/bolt_b200.h"
+#include "common.cuh"
+#include "kernels.h"
+
+namespace bolt {
+
+__device__ unsigned g_status = 0;
+
+namespace {
+
+thread_local std::string g_last_error;
+
+struct Options {
+  std::atomic<int> pdl{0};
+  std::atomic<int> early{0};
+  std::atomic<int64_t> budget{0};
+  Options() {
+    if (const char* v = std::getenv("BOLT_PDL")) pdl = std::atoi(v) != 0;
+    if (const char* v = std::getenv("BOLT_EARLY_WEIGHTS")) early = std::atoi(v) != 0;
+    if (const char* v = std::getenv("BOLT_SMEM_BUDGET")) budget = std::atoll(v);
+  }
+};
+
+Options& options() {
+  static Options o;
+  return o;
+}
+
+int sm_count() {
+  static std::mutex mu;
+  static int cache[64] = {0};
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return 148;
+  std::lock_guard<std::mutex> lock(mu);
+  if (cache[dev] == 0) {
+    int n = 0;
+    if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || n <= 0) n = 148;
+    cache[dev] = n;
+  }
+  return cache[dev];
+}
+
+LaunchCfg make_cfg(void* stream) {
+  LaunchCfg c;
+  c.stream = static_cast<cudaStream_t>(stream);
+  c.sms = sm_count();
+  c.pdl = options().pdl.load() != 0;
+  c.early_weights = c.pdl && options().early.load() != 0;
+  const int64_t b = options().budget.load();
+  if (b > 0) c.smem_budget = static_cast<size_t>(b);
+  return c;
+}
+
+struct Shape {
+  const int64_t* d;
+  int rank;
+  int64_t dim(int i) const {
+    if (i < 0 || i >= rank) throw std::invalid_argument("tensor rank too small");
+    return d[i];
+  }
+  int64_t count() const {
+    int64_t n = 1;
+    for (int i = 0; i < rank; ++i) n *= d[i];
+    return n;
+  }
+  int64_t last() const { return dim(rank - 1); }
+};
+
+void check_launch(cudaError_t e) {
+  if (e == cudaSuccess) e = cudaGetLastError();
+  if (e != cudaSuccess) throw std::runtime_error(cudaGetErrorString(e));
+}
+
+template <typename F>
+int guarded(F&& f) {
+  try {
+    f();
+    g_last_error.clear();
+    return BOLT_OK;
+  } catch (const std::exception& e) {
+    g_last_error = e.what();
+    return BOLT_FAIL;
+  }
+}
+
+void require(bool ok, const char* msg) {
+  if (!ok) throw std::invalid_argument(msg);
+}
+
+bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; }
+
+// The vectorised activation loads and the bulk copies of weight rows need 16-byte aligned
+// tensors (ORT and torch allocations always are).
+void require_aligned(std::initializer_list<const void*> ps, const char* op) {
+  for (const void* p : ps)
+    if (!aligned16(p)) throw std::invalid_argument(std::string(op) + ": tensors must be 16-byte aligned");
+}
+
+__global__ void f32_to_bf16_kernel(const float* __restrict__ in, bf16* __restrict__ out, int64_t n) {
+  pdl_trigger();
+  pdl_wait();
+  const int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+  if (i < n) out[i] = __float2bfloat16(in[i]);
+}
+
+int moe_verify_impl(const void* z, const int64_t* z_shape, int z_rank, const void* idx, const void* w,
+                    const void* fc1_w, const int64_t* fc1_w_shape, int fc1_w_rank, const void* fc1_s,
+                    const void* fc2_w, const void* fc2_s, int64_t topk, int64_t iq2, int64_t e_begin, int64_t e_end,
+                    bool sharded, void* out, void* h, void* part, void* meta, void* out_partial, void* stream) {
+  return guarded([&] {
+    const Shape zs{z_shape, z_rank}, w1s{fc1_w_shape, fc1_w_rank};
+    const int64_t R = zs.dim(0);
+    const int64_t P = R * topk;
+    // src/bolt_ops.cu:1193-1196
+    require(R >= 1 && R <= 8 && P <= 128 && topk >= 1, "MoeVerify: rows must be in [1,8] and rows*topk <= 128");
+    require(zs.dim(1) == 1024, "MoeVerify: latent size must be 1024");
+    const int64_t I = w1s.dim(1);
+    require(I % 64 == 0, "MoeVerify: inter size must be a multiple of 64");
+    require(iq2 != 2 || I % 256 == 0, "MoeVerify iq2=2: inter size must be a multiple of 256");
+    require(I <= 8192, "MoeVerify: inter size must be <= 8192");
+    const int64_t E = w1s.dim(0);
+    if (!sharded) {
+      e_begin = 0;
+      e_end = E;
+    }
+    require(e_begin >= 0 && e_begin <= e_end && e_end <= E, "MoeVerify: expert range outside [0, E]");
+    const int fmt = iq2 == 2 ? kFmtIq2N : (iq2 ? kFmtIq2Lut : kFmtQ4);
+    require_aligned({z, fc1_w, fc2_w}, "MoeVerify");
+    check_launch(launch_moe_verify(fmt, static_cast<const bf16*>(z), static_cast<const int*>(idx),
+                                   static_cast<const float*>(w), static_cast<const uint8_t*>(fc1_w),
+                                   static_cast<const bf16*>(fc1_s), static_cast<const uint8_t*>(fc2_w),
+                                   static_cast<const bf16*>(fc2_s), static_cast<int>(R), static_cast<int>(E),
+                                   static_cast<int>(I), static_cast<int>(topk), static_cast<int>(e_begin),
+                                   static_cast<int>(e_end), static_cast<bf16*>(out), static_cast<bf16*>(h),
+                                   static_cast<float*>(part), static_cast<int*>(meta), static_cast<float*>(out_partial),
+                                   make_cfg(stream)));
+  });
+}
+
+}  // namespace
+}  // namespace bolt
+
+using namespace bolt;
+
+extern "C" {
+
+const char* bolt_last_error(void) { return g_last_error.c_str(); }
+
+int bolt_abi_version(void) { return 100; }
+
+int bolt_set_launch_options(int pdl, int early_weights, int64_t smem_budget) {
+  options().pdl = pdl != 0;
+  options().early = early_weights != 0;
+  options().budget = smem_budget > 0 ? smem_budget : 0;
+  return BOLT_OK;
+}
+
+int bolt_get_device_status(unsigned* status) {
+  return guarded([&] {
+    unsigned v = 0, zero = 0;
+    check_launch(cudaDeviceSynchronize());
+    check_launch(cudaMemcpyFromSymbol(&v, g_status, sizeof(v)));
+    check_launch(cudaMemcpyToSymbol(g_status, &zero, sizeof(zero)));
+    if (status) *status = v;
+  });
+}
+
+int bolt_nvfp4_gemv(const void* x, const int64_t* x_shape, int x_rank, const void* w, const int64_t* w_shape,
+                    int w_rank, const void* w_scale, const void* g, void* y, void* stream) {
+  return guarded([&] {
+    const Shape xs{x_shape, x_rank}, ws{w_shape, w_rank};
+    const int64_t K = xs.last();
+    const int64_t R = K > 0 ? xs.count() / K : 0;
+    const int64_t N = ws.dim(0);
+    // src/bolt_ops.cu:1271, :1298
+    require(ws.dim(1) * 2 == K && K % 1024 == 0 && K > 0, "Nvfp4Gemv: K mismatch (K % 1024 required)");
+    require(R >= 1 && R <= 8, "Nvfp4Gemv: rows must be in [1,8]");
+    require_aligned({x, w}, "Nvfp4Gemv");
+    require(K <= 8192, "Nvfp4Gemv: K must be <= 8192");
+    check_launch(launch_gemv_mma(kFmtFp4, static_cast<const bf16*>(x), static_cast<int>(R),
+                                 static_cast<const uint8_t*>(w), w_scale, static_cast<const float*>(g), N,
+                                 static_cast<int>(K), static_cast<bf16*>(y), make_cfg(stream)));
+  });
+}
+
+static int qgemv(int bits, const void* x, const int64_t* x_shape, int x_rank, const void* B, const int64_t* B_shape,
+                 int B_rank, const void* scales, int64_t iq2, void* y, void* stream) {
+  return guarded([&] {
+    const Shape xs{x_shape, x_rank}, bs{B_shape, B_rank};
+    const int64_t K = xs.last();
+    const int64_t R = K > 0 ? xs.count() / K : 0;
+    const int64_t N = bs.dim(0);
+    if (bits == 8) iq2 = 0;  // Q8Gemv has no iq2 attribute (src/bolt_ops.cu:1433)
+    // src/bolt_ops.cu:1443-1451
+    if (iq2 == 2) {
+      require(K % 256 == 0 && B_rank >= 3 && bs.dim(1) * 32 == K && bs.dim(2) == 8 && R >= 1 && R <= 8,
+              "Q4Gemv iq2=2: needs B [N, K/32, 8] and 1..8 rows");
+    } else {
+      require(K % 32 == 0 && K > 0 && bs.dim(1) * 32 == K, "QGemv: K mismatch");
+    }
+    require(!(iq2 && iq2 != 2) || (R >= 2 && R <= 8 && K % 128 == 0), "Q4Gemv iq2: needs 2..8 rows and K % 128 == 0");
+    require(R >= 1 && R <= 8, "QGemv: rows must be in [1,8]");
+    if (iq2 || (R >= 2 && K % 64 == 0)) {
+      require_aligned({x, B}, bits == 8 ? "Q8Gemv" : "Q4Gemv");
+      require(K <= 8192, "QGemv: K must be <= 8192 for 2..8 rows and for iq2 modes");
+    }
+    const LaunchCfg cfg = make_cfg(stream);
+    const bf16* xb = static_cast<const bf16*>(x);
+    const uint8_t* wb = static_cast<const uint8_t*>(B);
+    bf16* yb = static_cast<bf16*>(y);
+    cudaError_t e;
+    if (iq2 == 2) {
+      e = launch_gemv_mma(kFmtIq2N, xb, static_cast<int>(R), wb, scales, nullptr, N, static_cast<int>(K), yb, cfg);
+    } else if (iq2) {
+      e = launch_gemv_mma(kFmtIq2Lut, xb, static_cast<int>(R), wb, scales, nullptr, N, static_cast<int>(K), yb, cfg);
+    } else if (R >= 2 && K % 64 == 0) {
+      e = launch_gemv_mma(bits == 8 ? kFmtQ8 : kFmtQ4, xb, static_cast<int>(R), wb, scales, nullptr, N,
+                          static_cast<int>(K), yb, cfg);
+    } else {
+      e = launch_gemv_exact(bits, xb, static_cast<int>(R), wb, static_cast<const bf16*>(scales), N,
+                            static_cast<int>(K), yb, cfg);
+    }
+    check_launch(e);
+  });
+}
+
+int bolt_q8_gemv(const void* x, const int64_t* x_shape, int x_rank, const void* B, const int64_t* B_shape, int B_rank,
+                 const void* scales, void* y, void* stream) {
+  return qgemv(8, x, x_shape, x_rank, B, B_shape, B_rank, scales, 0, y, stream);
+}
+
+int bolt_q4_gemv(const void* x, const int64_t* x_shape, int x_rank, const void* B, const int64_t* B_shape, int B_rank,
+                 const void* scales, int64_t iq2, void* y, void* stream) {
+  return qgemv(4, x, x_shape, x_rank, B, B_shape, B_rank, scales, iq2, y, stream);
+}
+
+int bolt_moe_route(const void* x, const int64_t* x_shape, int x_rank, const void* gate_w, const int64_t* gw_shape,
+                   int gw_rank, const void* bias, int64_t topk, float scale, void* idx, void* w, void* scores,
+                   void* stream) {
+  return guarded([&] {
+    const Shape xs{x_shape, x_rank}, gs{gw_shape, gw_rank};
+    const int64_t R = xs.dim(0), K = xs.dim(1), E = gs.dim(0);
+    // src/bolt_ops.cu:458
+    require(E <= 512 && K % 256 == 0 && topk <= 32 && topk >= 1 && E >= 1 && K > 0, "MoeRoute: unsupported shape");
+    if (R == 0) return;
+    require_aligned({x, gate_w}, "MoeRoute");
+    check_launch(launch_moe_route(static_cast<const bf16*>(x), static_cast<const bf16*>(gate_w),
+                                  static_cast<const float*>(bias), static_cast<int>(R), static_cast<int>(K),
+                                  static_cast<int>(E), static_cast<int>(topk), scale, static_cast<int*>(idx),
+                                  static_cast<float*>(w), static_cast<float*>(scores), make_cfg(stream)));
+  });
+}
+
+int bolt_moe_decode(const void* z, const int64_t* z_shape, int z_rank, const void* idx, const void* w,
+                    const void* fc1_w, const int64_t* fc1_w_shape, int fc1_w_rank, const void* fc1_s, const void* fc2_w,
+                    const void* fc2_s, int64_t topk, void* out, void* h, void* part, void* stream) {
+  return guarded([&] {
+    const Shape zs{z_shape, z_rank}, w1s{fc1_w_shape, fc1_w_rank};
+    const int64_t R = zs.dim(0);
+    // src/bolt_ops.cu:601-603
+    require(zs.dim(1) == 1024, "MoeDecode: latent size must be 1024");
+    const int64_t I = w1s.dim(1);
+    require(I % 32 == 0 && I % 8 == 0 && I > 0, "MoeDecode: bad inter size");
+    require(topk >= 1 && R * topk <= 128, "MoeDecode: rows*topk must be in [1,128]");
+    if (R == 0) return;
+    require_aligned({z, fc1_w, fc2_w}, "MoeDecode");
+    check_launch(launch_moe_decode(static_cast<const bf16*>(z), static_cast<const int*>(idx),
+                                   static_cast<const float*>(w), static_cast<const uint8_t*>(fc1_w),
+                                   static_cast<const bf16*>(fc1_s), static_cast<const uint8_t*>(fc2_w),
+                                   static_cast<const bf16*>(fc2_s), static_cast<int>(R), static_cast<int>(w1s.dim(0)),
+                                   static_cast<int>(I), static_cast<int>(topk), static_cast<bf16*>(out),
+                                   static_cast<bf16*>(h), static_cast<float*>(part), make_cfg(stream)));
+  });
+}
+
+int bolt_moe_verify(const void* z, const int64_t* z_shape, int z_rank, const void* idx, const void* w,
+                    const void* fc1_w, const int64_t* fc1_w_shape, int fc1_w_rank, const void* fc1_s, const void* fc2_w,
+                    const void* fc2_s, int64_t topk, int64_t iq2, void* out, void* h, void* part, void* meta,
+                    void* stream) {
+  return moe_verify_impl(z, z_shape, z_rank, idx, w, fc1_w, fc1_w_shape, fc1_w_rank, fc1_s, fc2_w, fc2_s, topk, iq2, 0,
+                         0, false, out, h, part, meta, nullptr, stream);
+}
+
+int bolt_moe_verify_shard(const void* z, const int64_t* z_shape, int z_rank, const void* idx, const void* w,
+                          const void* fc1_w, const int64_t* fc1_w_shape, int fc1_w_rank, const void* fc1_s,
+                          const void* fc2_w, const void* fc2_s, int64_t topk, int64_t iq2, int64_t e_begin,
+                          int64_t e_end, void* out, void* h, void* part, void* meta, void* out_partial, void* stream) {
+  return moe_verify_impl(z, z_shape, z_rank, idx, w, fc1_w, fc1_w_shape, fc1_w_rank, fc1_s, fc2_w, fc2_s, topk, iq2,
+                         e_begin, e_end, true, out, h, part, meta, out_partial, stream);
+}
+
+int bolt_f32_to_bf16(const void* in, void* out, int64_t n, void* stream) {
+  return guarded([&] {
+    require(n >= 0, "bolt_f32_to_bf16: negative size");
+    if (n == 0) return;
+    check_launch(launch_kernel(f32_to_bf16_kernel, dim3(static_cast<unsigned>((n + 255) / 256)), dim3(256), 0,
+                               make_cfg(stream), static_cast<const float*>(in), static_cast<bf16*>(out), n));
+  });
+}
+
+int bolt_dequant(int fmt, int exact, const void* w, const void* scales, int64_t N, int64_t K, void* out, void* stream) {
+  return guarded([&] {
+    require(fmt >= 0 && fmt <= 4, "bolt_dequant: unknown format");
+    require(!exact || fmt == kFmtQ8 || fmt == kFmtQ4, "bolt_dequant: exact contract exists for Q8 / Q4 only");
+    const int64_t kmod = fmt == kFmtIq2N ? 256 : fmt == kFmtFp4 ? 64 : 64;
+    require(N >= 0 && K > 0 && K % kmod == 0, "bolt_dequant: K must be a multiple of 64 (256 for IQ2_XXS)");
+    if (N == 0) return;
+    check_launch(launch_dequant(fmt, exact, static_cast<const uint8_t*>(w), scales, N, static_cast<int>(K),
+                                static_cast<float*>(out), make_cfg(stream)));
+  });
+}
+
+}  // extern "C"

@@ -1,0 +1,71 @@
+// Host-side launch interface of the bolt B200 kernels (internal to libbolt_b200.so).
+#pragma once
+
+#include <cuda_bf16.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include <algorithm>
+
+namespace bolt {
+
+using bf16 = __nv_bfloat16;
+
+// How a kernel is launched.  `pdl` adds the programmatic-stream-serialization attribute so a
+// kernel may start while the previous kernel of the stream drains; kernels still wait
+// (griddepcontrol.wait) before touching activations or outputs.  `early_weights` lets them
+// stream weights before that wait, which is only valid when the preceding kernel does not
+// write the weights (true for inference graphs, where weights are initializers).
+struct LaunchCfg {
+  cudaStream_t stream = nullptr;
+  int sms = 148;
+  bool pdl = false;
+  bool early_weights = false;
+  size_t smem_budget = 100 * 1024;  // ring bytes per CTA; ~half an SM so a PDL successor fits beside it
+};
+
+template <typename... KArgs, typename... Args>
+cudaError_t launch_kernel(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, const LaunchCfg& cfg,
+                          Args&&... args) {
+  cudaLaunchConfig_t lc = {};
+  lc.gridDim = grid;
+  lc.blockDim = block;
+  lc.dynamicSmemBytes = smem;
+  lc.stream = cfg.stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  lc.attrs = attr;
+  lc.numAttrs = cfg.pdl ? 1 : 0;
+  return cudaLaunchKernelEx(&lc, kernel, std::forward<Args>(args)...);
+}
+
+// ---- GEMV ------------------------------------------------------------------------------
+// Exact fp32-weight path (Q8 bits=8 / Q4 bits=4).
+cudaError_t launch_gemv_exact(int bits, const bf16* x, int R, const uint8_t* w, const bf16* sc, int64_t N, int K,
+                              bf16* y, const LaunchCfg& cfg);
+
+// Tensor-core path.  fmt: weight format (see Fmt in gemv_mma.cu).
+enum WeightFmt : int { kFmtQ8 = 0, kFmtQ4 = 1, kFmtFp4 = 2, kFmtIq2Lut = 3, kFmtIq2N = 4 };
+cudaError_t launch_gemv_mma(int fmt, const bf16* x, int R, const uint8_t* w, const void* sc, const float* gscale,
+                            int64_t N, int K, bf16* y, const LaunchCfg& cfg);
+
+// Debug: dequantise rows [0, N) with the exact contract of `fmt` (fp32 out) -- used by the
+// bit-exactness tests of the weight decode.
+cudaError_t launch_dequant(int fmt, int exact, const uint8_t* w, const void* sc, int64_t N, int K, float* out,
+                           const LaunchCfg& cfg);
+
+// ---- MoE -------------------------------------------------------------------------------
+cudaError_t launch_moe_route(const bf16* x, const bf16* gate_w, const float* bias, int R, int K, int E, int topk,
+                             float scale, int* idx, float* w, float* scores, const LaunchCfg& cfg);
+
+cudaError_t launch_moe_decode(const bf16* z, const int* idx, const float* w, const uint8_t* fc1_w, const bf16* fc1_s,
+                              const uint8_t* fc2_w, const bf16* fc2_s, int R, int E, int I, int topk, bf16* out,
+                              bf16* h, float* part, const LaunchCfg& cfg);
+
+cudaError_t launch_moe_verify(int fmt, const bf16* z, const int* idx, const float* w, const uint8_t* fc1_w,
+                              const bf16* fc1_s, const uint8_t* fc2_w, const bf16* fc2_s, int R, int E, int I,
+                              int topk, int e_begin, int e_end, bf16* out, bf16* h, float* part, int* meta,
+                              float* out_partial, const LaunchCfg& cfg);
+
+}  // namespace bolt

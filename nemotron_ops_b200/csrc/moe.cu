@@ -1,0 +1,745 @@
+// MoeRoute / MoeDecode / MoeVerify kernels (reference src/bolt_ops.cu:359-619, :1078-1257).
+//
+// MoeRoute: the fp32 router logits are one streaming dot per expert spread over all SMs (each
+// warp reads one gate row once and applies it to every activation row); the selection is one
+// warp per row: `topk` rounds of warp arg-max over score + bias with ties to the lower index.
+//
+// MoeDecode (exact fp32 weight contract, int4 zp 8): two persistent kernels chained with
+// programmatic dependent launch.  Both treat the P = R * topk (token, expert) pairs as
+// segments and give every CTA the same row range of every segment, so all CTAs stream the
+// same number of bytes.  fc1 writes h = bf16(relu(bf16(z . W1))^2); fc2 computes
+// part = float(bf16(h . W2)) for its output rows of every pair and finishes those rows of
+// `out` itself (the finalize needs no third kernel).  fc2 starts streaming its weights while
+// fc1 is still running.
+//
+// MoeVerify (tensor-core weight contract): a one-CTA grouping kernel writes the reference's
+// `meta` layout; the expert GEMMs run over a device-side work list of (unique expert, 16-row
+// tile) items sized from meta[0], so no CTA is launched for experts that were not selected.
+#include "mma_decode.cuh"
+
+namespace bolt {
+
+namespace {
+
+// =======================================================================================
+// MoeRoute
+// =======================================================================================
+// one warp per expert; lanes stride over K in 16-byte vectors; every activation row reuses
+// the gate row held in registers (K <= 8192 -> 32 x 16 B per lane at most)
+template <int RMAX>
+__global__ void __launch_bounds__(128) router_logits_kernel(const bf16* __restrict__ x, const bf16* __restrict__ gw,
+                                                            int R, int K, int E, float* __restrict__ scores) {
+  pdl_trigger();
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int e = blockIdx.x * 4 + warp;
+  pdl_wait();
+  if (e >= E) return;
+  const bf16* wr = gw + static_cast<int64_t>(e) * K;
+  const int nv = K >> 8;  // 16-byte vectors per lane (K % 256 == 0)
+  for (int r0 = 0; r0 < R; r0 += RMAX) {
+    float acc[RMAX];
+#pragma unroll
+    for (int r = 0; r < RMAX; ++r) acc[r] = 0.f;
+    for (int v = 0; v < nv; ++v) {
+      const int k = (v * 32 + lane) * 8;
+      const uint4 wv = __ldg(reinterpret_cast<const uint4*>(wr + k));
+      const uint32_t ww[4] = {wv.x, wv.y, wv.z, wv.w};
+#pragma unroll
+      for (int r = 0; r < RMAX; ++r) {
+        if (r0 + r < R) {
+          const uint4 xv = __ldg(reinterpret_cast<const uint4*>(x + static_cast<int64_t>(r0 + r) * K + k));
+          const uint32_t xx[4] = {xv.x, xv.y, xv.z, xv.w};
+#pragma unroll
+          for (int q = 0; q < 4; ++q) {
+            acc[r] = fmaf(__uint_as_float(ww[q] << 16), __uint_as_float(xx[q] << 16), acc[r]);
+            acc[r] = fmaf(__uint_as_float(ww[q] & 0xFFFF0000u), __uint_as_float(xx[q] & 0xFFFF0000u), acc[r]);
+          }
+        }
+      }
+    }
+#pragma unroll
+    for (int r = 0; r < RMAX; ++r) {
+      const float a = warp_sum(acc[r]);
+      if (lane == 0 && r0 + r < R) scores[static_cast<int64_t>(r0 + r) * E + e] = 1.0f / (1.0f + expf(-a));
+    }
+  }
+}
+
+// one warp per row, E <= 512 (16 candidates per lane)
+__global__ void __launch_bounds__(32) router_topk_kernel(const float* __restrict__ scores, const float* __restrict__ bias,
+                                                          int E, int topk, float scale, int* __restrict__ idx,
+                                                          float* __restrict__ wout) {
+  pdl_trigger();
+  pdl_wait();
+  const int r = blockIdx.x, lane = threadIdx.x;
+  float val[16], sc[16];
+#pragma unroll
+  for (int i = 0; i < 16; ++i) {
+    const int e = i * 32 + lane;
+    if (e < E) {
+      sc[i] = scores[static_cast<int64_t>(r) * E + e];
+      val[i] = sc[i] + bias[e];
+    } else {
+      sc[i] = 0.f;
+      val[i] = -INFINITY;
+    }
+  }
+  int my_idx = -1;
+  float my_sc = 0.f, total = 0.f;
+  for (int j = 0; j < topk; ++j) {
+    float bv = -INFINITY;
+    int bi = 0x7fffffff;
+    float bs = 0.f;
+#pragma unroll
+    for (int i = 0; i < 16; ++i)  // ascending expert id per lane: strict > keeps the lowest id on ties
+      if (val[i] > bv) { bv = val[i]; bi = i * 32 + lane; bs = sc[i]; }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+      const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
+      const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
+      const float os = __shfl_xor_sync(0xffffffffu, bs, o);
+      if (ov > bv || (ov == bv && oi < bi)) { bv = ov; bi = oi; bs = os; }
+    }
+    const bool found = bv > -INFINITY;
+    if (found && (bi & 31) == lane) {
+#pragma unroll
+      for (int i = 0; i < 16; ++i)
+        if (i == (bi >> 5)) val[i] = -INFINITY;
+    }
+    const float s = found ? bs : 0.f;
+    if (lane == j) { my_idx = found ? bi : -1; my_sc = s; }
+    total += s;
+  }
+  const float denom = total + 1e-20f;
+  if (lane < topk) {
+    idx[r * topk + lane] = my_idx;
+    wout[r * topk + lane] = my_sc / denom * scale;
+  }
+}
+
+// =======================================================================================
+// MoeDecode: segmented exact-weight streaming GEMV (int4, zero point 8, bf16 block-32 scales)
+// =======================================================================================
+constexpr int kSegWarps = 8;
+constexpr int kSegThreads = kSegWarps * 32;
+constexpr int kSegRows = 8;  // rows per stage
+constexpr int kMaxPairs = 128;
+
+struct SegParams {
+  const bf16* x;         // fc1: z [R, K]; fc2: h [P, K]
+  const int* idx;        // [P] expert ids
+  const float* w;        // [P] routing weights (fc2 finalize)
+  const uint8_t* wq;     // [E, Nseg, K/2]
+  const bf16* sc;        // [E, Nseg, K/32]
+  bf16* h_out;           // fc1 output [P, Nseg]
+  float* part_out;       // fc2 output [P, Nseg]
+  bf16* out;             // fc2 finalize output [R, Nseg]
+  int P, topk, E, Nseg, K;
+  int nstage;
+  uint32_t stage_bytes;
+  int early_weights;
+};
+
+// stage s of a CTA: segment p = s / spp, rows [a + (s % spp) * 8, ...) of that segment
+struct SegRange {
+  int a, b, spp;
+};
+
+__device__ __forceinline__ SegRange seg_range(const SegParams& p) {
+  SegRange r;
+  r.a = static_cast<int>(static_cast<int64_t>(blockIdx.x) * p.Nseg / gridDim.x);
+  r.b = static_cast<int>(static_cast<int64_t>(blockIdx.x + 1) * p.Nseg / gridDim.x);
+  r.spp = (r.b - r.a + kSegRows - 1) / kSegRows;
+  return r;
+}
+
+// Reads at L2 (the coherence point): kernels that start early under programmatic dependent
+// launch read values produced before their primary's wait this way, never from L1.
+__device__ __forceinline__ int ld_cg(const int* p) {
+  int v;
+  asm volatile("ld.global.cg.s32 %0, [%1];" : "=r"(v) : "l"(p));
+  return v;
+}
+
+__device__ __forceinline__ int load_expert(const int* idx, int pp) { return ld_cg(idx + pp); }
+
+__device__ __forceinline__ void seg_issue(const SegParams& p, uint8_t* smem, uint64_t* full_bar, const SegRange& rg,
+                                          int s, int e) {
+  const int slot_i = s % p.nstage;
+  const int pp = s / rg.spp;
+  const int row = rg.a + (s % rg.spp) * kSegRows;
+  const int rows = min(kSegRows, rg.b - row);
+  uint8_t* slot = smem + static_cast<size_t>(slot_i) * p.stage_bytes;
+  const uint32_t fb = smem_u32(&full_bar[slot_i]);
+  uint32_t tx = 0;
+  if (e >= 0 && e < p.E && rows > 0) {
+    const int64_t rb = p.K / 2;
+    const int nb = p.K / 32;
+    const int64_t grow = static_cast<int64_t>(e) * p.Nseg + row;
+    bulk_g2s(smem_u32(slot), p.wq + grow * rb, static_cast<uint32_t>(rows * rb), fb);
+    tx += static_cast<uint32_t>(rows * rb);
+    const uint8_t* scb = reinterpret_cast<const uint8_t*>(p.sc);
+    stage_span(slot + kSegRows * rb, scb + grow * nb * 2, rows * nb * 2, scb + static_cast<int64_t>(p.E) * p.Nseg * nb * 2,
+               fb, tx);
+  }
+  mbar_arrive_expect_tx(fb, tx);
+}
+
+// FC: 1 = fc1 (relu2 -> h), 2 = fc2 (part, then this CTA's rows of out)
+template <int FC, int TPR, int SPT>
+__global__ void __launch_bounds__(kSegThreads, 1) moe_seg_kernel(const SegParams p) {
+  extern __shared__ __align__(128) uint8_t smem[];
+  constexpr int RP = kSegThreads / TPR;
+  constexpr int NP = kSegRows / RP;
+  __shared__ uint64_t full_bar[16];
+  __shared__ float red[2][kSegWarps][kSegRows];
+  __shared__ int experts[kMaxPairs];
+  __shared__ float part_s[FC == 2 ? kMaxPairs * kSegRows * 2 : 1];
+  __shared__ volatile int abort_flag;
+
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const SegRange rg = seg_range(p);
+  const int nst = rg.spp * p.P;
+  const int NS = p.nstage;
+  const int K = p.K;
+  const int nb = K >> 5;
+  const int64_t rb = K / 2;
+
+  if (tid == 0) {
+    for (int s = 0; s < NS; ++s) mbar_init(smem_u32(&full_bar[s]), 1);
+    abort_flag = 0;
+    fence_barrier_init();
+  }
+  __syncthreads();
+  if (FC == 1) {
+    // the routing ids are this op's inputs: wait for the producer of those before reading
+    pdl_wait();
+    pdl_trigger();
+  } else {
+    pdl_trigger();
+    if (!p.early_weights) pdl_wait();
+  }
+  for (int i = tid; i < p.P; i += kSegThreads) experts[i] = load_expert(p.idx, i);
+  __syncthreads();
+  if (tid == 0)
+    for (int s = 0; s < min(NS, nst); ++s) seg_issue(p, smem, full_bar, rg, s, experts[s / rg.spp]);
+  pdl_wait();
+
+  const int grp = tid / TPR, pt = tid % TPR;
+  const int nslots = K >> 4;
+  float2 xv[SPT][8];
+  float xoff[SPT];
+  int xsrc = -1;  // activation row currently held in registers
+
+  for (int s = 0; s < nst; ++s) {
+    const int slot_i = s % NS;
+    const uint32_t ph = (s / NS) & 1;
+    const int pp = s / rg.spp;
+    const int row0 = rg.a + (s % rg.spp) * kSegRows;
+    const int rows = min(kSegRows, rg.b - row0);
+    const int e = experts[pp];
+    const bool live = e >= 0 && e < p.E;
+    if (!abort_flag && !mbar_wait(smem_u32(&full_bar[slot_i]), ph, kStatusFullWait)) abort_flag = 1;
+    const int src = (FC == 1) ? pp / p.topk : pp;
+    if (live && src != xsrc) {
+      xsrc = src;
+#pragma unroll
+      for (int j = 0; j < SPT; ++j) {
+        const int slot = pt + j * TPR;
+        float xf[16];
+        if (slot < nslots) {
+          const uint4* xp = reinterpret_cast<const uint4*>(p.x + static_cast<int64_t>(src) * K + slot * 16);
+          const uint4 a = xp[0], b = xp[1];
+          const uint32_t u[8] = {a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w};
+#pragma unroll
+          for (int i = 0; i < 8; ++i) {
+            xf[2 * i] = __uint_as_float(u[i] << 16);
+            xf[2 * i + 1] = __uint_as_float(u[i] & 0xFFFF0000u);
+          }
+        } else {
+#pragma unroll
+          for (int i = 0; i < 16; ++i) xf[i] = 0.f;
+        }
+#pragma unroll
+        for (int q = 0; q < 2; ++q) {
+          xv[j][4 * q + 0] = make_float2(xf[8 * q + 0], xf[8 * q + 2]);
+          xv[j][4 * q + 1] = make_float2(xf[8 * q + 4], xf[8 * q + 6]);
+          xv[j][4 * q + 2] = make_float2(xf[8 * q + 1], xf[8 * q + 3]);
+          xv[j][4 * q + 3] = make_float2(xf[8 * q + 5], xf[8 * q + 7]);
+        }
+        float sum = 0.f;
+#pragma unroll
+        for (int i = 0; i < 16; ++i) sum += xf[i];
+        xoff[j] = -136.f * sum;
+      }
+    }
+    const uint8_t* slot_w = smem + static_cast<size_t>(slot_i) * p.stage_bytes;
+    const int64_t grow = static_cast<int64_t>(live ? e : 0) * p.Nseg + row0;
+    const uint8_t* slot_sc = slot_w + kSegRows * rb + (reinterpret_cast<uintptr_t>(p.sc + grow * nb) & 15);
+
+    float part[NP];
+#pragma unroll
+    for (int u = 0; u < NP; ++u) {
+      const int rl = u * RP + grp;
+      float acc = 0.f;
+      if (live && rl < rows) {
+        const uint8_t* wrow = slot_w + rl * rb;
+        const bf16* srow = reinterpret_cast<const bf16*>(slot_sc) + rl * nb;
+#pragma unroll
+        for (int j = 0; j < SPT; ++j) {
+          const int slot = pt + j * TPR;
+          if (slot < nslots) {
+            const float scv = __bfloat162float(srow[slot >> 1]);
+            const uint2 wv = *reinterpret_cast<const uint2*>(wrow + slot * 8);
+            const uint32_t M = 0x3F000000u;
+            const uint32_t wd[2] = {wv.x, wv.y};
+            float2 a = make_float2(0.f, 0.f), b = make_float2(0.f, 0.f);
+#pragma unroll
+            for (int q = 0; q < 2; ++q) {
+              const uint32_t lo = wd[q] & 0x0F0F0F0Fu, hi = (wd[q] >> 4) & 0x0F0F0F0Fu;
+              a = ffma2(make_float2(__uint_as_float(prmt(lo, M, 0x7044)), __uint_as_float(prmt(lo, M, 0x7144))),
+                        xv[j][4 * q + 0], a);
+              b = ffma2(make_float2(__uint_as_float(prmt(lo, M, 0x7244)), __uint_as_float(prmt(lo, M, 0x7344))),
+                        xv[j][4 * q + 1], b);
+              a = ffma2(make_float2(__uint_as_float(prmt(hi, M, 0x7044)), __uint_as_float(prmt(hi, M, 0x7144))),
+                        xv[j][4 * q + 2], a);
+              b = ffma2(make_float2(__uint_as_float(prmt(hi, M, 0x7244)), __uint_as_float(prmt(hi, M, 0x7344))),
+                        xv[j][4 * q + 3], b);
+            }
+            const float S = (a.x + a.y) + (b.x + b.y);
+            acc = fmaf(fmaf(256.f, S, xoff[j]), scv, acc);
+          }
+        }
+      }
+      part[u] = acc;
+    }
+    // reduce-scatter over lanes, then across the warps of each row group
+    {
+      int o = 16;
+#pragma unroll
+      for (int n = NP; n > 1; n >>= 1, o >>= 1) {
+        const bool upper = (lane & o) != 0;
+#pragma unroll
+        for (int i = 0; i < n / 2; ++i) {
+          const float send = upper ? part[i] : part[i + n / 2];
+          const float keep = upper ? part[i + n / 2] : part[i];
+          part[i] = keep + __shfl_xor_sync(0xffffffffu, send, o);
+        }
+      }
+#pragma unroll
+      for (; o >= 1; o >>= 1) part[0] += __shfl_xor_sync(0xffffffffu, part[0], o);
+    }
+    constexpr int kLanesPerRow = 32 / NP;
+    constexpr int kLog2NP = NP == 8 ? 3 : NP == 4 ? 2 : NP == 2 ? 1 : 0;
+    const int buf = s & 1;
+    if ((lane & (kLanesPerRow - 1)) == 0) red[buf][warp][((lane >> (5 - kLog2NP)) & (NP - 1)) * RP + grp] = part[0];
+    asm volatile("bar.sync 1;" ::: "memory");
+    if (tid == 0 && s + NS < nst && !abort_flag) seg_issue(p, smem, full_bar, rg, s + NS, experts[(s + NS) / rg.spp]);
+    if (tid < rows) {
+      const int rl = tid;
+      const int gg = rl % RP;
+      constexpr int WPG = TPR / 32;
+      float tsum = 0.f;
+#pragma unroll
+      for (int w = 0; w < WPG; ++w) tsum += red[buf][gg * WPG + w][rl];
+      const int64_t o = static_cast<int64_t>(pp) * p.Nseg + row0 + rl;
+      const float bfv = __bfloat162float(__float2bfloat16(tsum));
+      if (FC == 1) {
+        const float r = live ? fmaxf(bfv, 0.f) : 0.f;
+        p.h_out[o] = __float2bfloat16(r * r);
+      } else {
+        const float v = live ? bfv : 0.f;
+        p.part_out[o] = v;
+        part_s[pp * kSegRows * 2 + (s % rg.spp) * kSegRows + rl] = v;
+      }
+    }
+  }
+  if constexpr (FC == 2) {
+    // out[t, n] = bf16(sum_k w[t, k] * part[t * topk + k, n]) for this CTA's rows, k ascending
+    __syncthreads();
+    const int R = p.P / p.topk;
+    const int nrow = rg.b - rg.a;
+    for (int i = tid; i < R * nrow; i += kSegThreads) {
+      const int t = i / nrow, rl = i % nrow;
+      float a = 0.f;
+      for (int k = 0; k < p.topk; ++k) {
+        const int pp = t * p.topk + k;
+        a = fmaf(p.w[pp], part_s[pp * kSegRows * 2 + rl], a);
+      }
+      p.out[static_cast<int64_t>(t) * p.Nseg + rg.a + rl] = __float2bfloat16(a);
+    }
+  }
+  if (tid == 0 && abort_flag)
+    for (int s = max(0, nst - NS); s < nst; ++s) mbar_wait(smem_u32(&full_bar[s % NS]), (s / NS) & 1, kStatusDrainWait);
+}
+
+// =======================================================================================
+// MoeVerify
+// =======================================================================================
+// meta: [0] = U, [1 .. P] = unique expert ids in first-occurrence order (unused slots -1),
+// [1 + P + u * 8 + row] = pair index of `row` for unique expert u, or -1.
+// Experts outside [e_begin, e_end) (the shard's range; the whole [0, E) unsharded) are left
+// out of the list.
+__global__ void __launch_bounds__(128) moe_group_kernel(const int* __restrict__ idx, int P, int topk, int e_begin,
+                                                        int e_end, int* __restrict__ meta) {
+  __shared__ int sid[kMaxPairs];
+  __shared__ int srank[kMaxPairs];
+  __shared__ int wtot[4];
+  pdl_wait();
+  pdl_trigger();
+  const int p = threadIdx.x, lane = p & 31, warp = p >> 5;
+  for (int i = p; i < 8 * P + P; i += blockDim.x) meta[1 + i] = -1;
+  const int e = p < P ? idx[p] : -1;
+  if (p < P) sid[p] = e;
+  __syncthreads();
+  const bool local = p < P && e >= e_begin && e < e_end;
+  int first = -1;
+  if (local) {
+    for (int j = 0; j <= p; ++j)
+      if (sid[j] == e) { first = j; break; }
+  }
+  const bool lead = local && first == p;
+  const unsigned bal = __ballot_sync(0xffffffffu, lead);
+  if (lane == 0) wtot[warp] = __popc(bal);
+  __syncthreads();
+  int off = 0;
+  for (int w = 0; w < warp; ++w) off += wtot[w];
+  if (lead) srank[p] = off + __popc(bal & ((1u << lane) - 1u));
+  __syncthreads();  // the -1 fill above is complete before the writes below (same threads' order
+                    // is not enough: another thread may own the slot)
+  if (lead) meta[1 + srank[p]] = e;
+  if (local) meta[1 + P + srank[first] * 8 + p / topk] = p;
+  if (p == 0) meta[0] = wtot[0] + wtot[1] + wtot[2] + wtot[3];
+}
+
+constexpr int kTile = 16;
+
+struct VerifyParams {
+  const bf16* xin;       // fc1: z [R, K]; fc2: h [P, K]
+  const int* meta;
+  const uint8_t* wq;     // [E, Nrows, row_bytes]
+  const uint8_t* sc;     // [E, Nrows, sc_row_bytes]
+  void* out;             // fc1: h bf16 [P, Nrows]; fc2: part f32 [P, Nrows]
+  int P, R, E, Nrows, K;
+  int nstage;
+  uint32_t stage_bytes;
+  uint32_t row_stride;
+  int early_weights;
+};
+
+// work item q: unique expert u = q / tpe, rows [16 * (q % tpe), +16) of that expert
+template <int FMT>
+__device__ __forceinline__ void verify_issue(const VerifyParams& p, uint8_t* smem, uint64_t* full_bar, int i, int q0,
+                                             int tpe, const int* uexp) {
+  const int slot_i = i % p.nstage;
+  const int q = q0 + i;
+  const int u = q / tpe;
+  const int n0 = (q % tpe) * kTile;
+  const int rows = min(kTile, p.Nrows - n0);
+  const int e = uexp[u];
+  const int64_t rb = fmt_row_bytes(FMT, p.K);
+  const int64_t srb = fmt_scale_row_bytes(FMT, p.K);
+  uint8_t* slot = smem + static_cast<size_t>(slot_i) * p.stage_bytes;
+  const uint32_t fb = smem_u32(&full_bar[slot_i]);
+  uint32_t tx = 0;
+  if (e >= 0 && e < p.E) {
+    const int64_t grow = static_cast<int64_t>(e) * p.Nrows + n0;
+    for (int r = 0; r < rows; ++r)
+      bulk_g2s(smem_u32(slot + r * p.row_stride), p.wq + (grow + r) * rb, static_cast<uint32_t>(rb), fb);
+    tx = static_cast<uint32_t>(rows * rb);
+    stage_span(slot + kTile * p.row_stride, p.sc + grow * srb, static_cast<uint32_t>(rows * srb),
+               p.sc + static_cast<int64_t>(p.E) * p.Nrows * srb, fb, tx);
+  }
+  mbar_arrive_expect_tx(fb, tx);
+}
+
+// PH 1: h[pair, j] = bf16(relu(bf16(z . W1[e, j]))^2); PH 2: part[pair, n] = float(bf16(h . W2[e, n]))
+template <int FMT, int PH, int KW, int CPW>
+__global__ void __launch_bounds__(KW * 32, 1) moe_verify_mma_kernel(const VerifyParams p) {
+  extern __shared__ __align__(128) uint8_t smem[];
+  __shared__ uint64_t full_bar[16];
+  __shared__ float red[2][KW][128];
+  __shared__ __align__(16) uint32_t grid_s[(FMT == kFmtIq2N) ? 1024 : 4];
+  __shared__ int uexp[kMaxPairs];
+  __shared__ int pmap[kMaxPairs][8];
+  __shared__ volatile int abort_flag;
+  __shared__ int s_u;
+
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int g = lane >> 2, t = lane & 3;
+  const int K = p.K;
+  const int tpe = (p.Nrows + kTile - 1) / kTile;
+  const int NS = p.nstage;
+  const int64_t srb = fmt_scale_row_bytes(FMT, K);
+
+  if (tid == 0) {
+    for (int s = 0; s < NS; ++s) mbar_init(smem_u32(&full_bar[s]), 1);
+    abort_flag = 0;
+    fence_barrier_init();
+  }
+  if constexpr (FMT == kFmtIq2N) {
+    for (int i = tid; i < 1024; i += blockDim.x) grid_s[i] = kIq2xxsGridBf16x2[i];
+  }
+  // PH 1 directly follows the grouping kernel, so it waits before reading the work list.  PH 2
+  // is released by PH 1 only after PH 1's own wait (meta complete), so it reads the work list
+  // (at L2) and starts streaming its weights while PH 1 still computes; it waits for PH 1's h
+  // before loading activations.
+  if (PH == 1) pdl_wait();
+  pdl_trigger();
+  if (tid == 0) s_u = ld_cg(p.meta);
+  for (int i = tid; i < p.P; i += blockDim.x) uexp[i] = ld_cg(p.meta + 1 + i);
+  for (int i = tid; i < p.P * 8; i += blockDim.x) pmap[i >> 3][i & 7] = ld_cg(p.meta + 1 + p.P + i);
+  __syncthreads();
+  const int U = s_u;
+  const int total = U * tpe;
+  const int q0 = static_cast<int>(static_cast<int64_t>(blockIdx.x) * total / gridDim.x);
+  const int q1 = static_cast<int>(static_cast<int64_t>(blockIdx.x + 1) * total / gridDim.x);
+  const int nq = q1 - q0;
+  if (tid == 0)
+    for (int i = 0; i < min(NS, nq); ++i) verify_issue<FMT>(p, smem, full_bar, i, q0, tpe, uexp);
+
+  if (PH == 2) pdl_wait();
+
+  const int nchunks = K >> 6;
+  const int cb = static_cast<int>(static_cast<int64_t>(warp) * nchunks / KW);
+  const int ce = static_cast<int>(static_cast<int64_t>(warp + 1) * nchunks / KW);
+  uint32_t bfr[CPW][8];
+  int xu = -1;  // unique expert whose activation rows are in bfr (PH 2)
+
+  for (int i = 0; i < nq; ++i) {
+    const int slot_i = i % NS;
+    const uint32_t ph = (i / NS) & 1;
+    const int q = q0 + i;
+    const int u = q / tpe;
+    const int n0 = (q % tpe) * kTile;
+    const int rows = min(kTile, p.Nrows - n0);
+    if ((PH == 1 && xu < 0) || (PH == 2 && u != xu)) {
+      xu = u;
+      int xrow;
+      bool valid;
+      if (PH == 1) {
+        xrow = g;
+        valid = g < p.R;
+      } else {
+        xrow = pmap[u][g];
+        valid = xrow >= 0;
+      }
+#pragma unroll
+      for (int j = 0; j < CPW; ++j) {
+        uint32_t x16[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+        const int c = cb + j;
+        if (c < ce && valid) {
+          const uint4* xp = reinterpret_cast<const uint4*>(p.xin + static_cast<int64_t>(xrow) * K + 64 * c + 16 * t);
+          const uint4 a = xp[0], b = xp[1];
+          x16[0] = a.x; x16[1] = a.y; x16[2] = a.z; x16[3] = a.w;
+          x16[4] = b.x; x16[5] = b.y; x16[6] = b.z; x16[7] = b.w;
+        }
+        make_b_frags<FMT>(x16, bfr[j]);
+      }
+    }
+    if (!abort_flag && !mbar_wait(smem_u32(&full_bar[slot_i]), ph, kStatusFullWait)) abort_flag = 1;
+    const uint8_t* slot = smem + static_cast<size_t>(slot_i) * p.stage_bytes;
+    const int e = uexp[u];
+    const int64_t grow = static_cast<int64_t>(e >= 0 ? e : 0) * p.Nrows + n0;
+    const uint8_t* sc_base = slot + kTile * p.row_stride + (reinterpret_cast<uintptr_t>(p.sc + grow * srb) & 15);
+    float acc[4] = {0.f, 0.f, 0.f, 0.f};
+    if (e >= 0 && e < p.E) {
+#pragma unroll
+      for (int j = 0; j < CPW; ++j)
+        if (cb + j < ce)
+          mma_chunk<FMT>(slot + g * p.row_stride, slot + (g + 8) * p.row_stride, sc_base + g * srb,
+                         sc_base + (g + 8) * srb, cb + j, t, grid_s, bfr[j], acc);
+    }
+    const int buf = i & 1;
+    *reinterpret_cast<float2*>(&red[buf][warp][g * 8 + 2 * t]) = make_float2(acc[0], acc[1]);
+    *reinterpret_cast<float2*>(&red[buf][warp][(g + 8) * 8 + 2 * t]) = make_float2(acc[2], acc[3]);
+    asm volatile("bar.sync 1;" ::: "memory");
+    if (tid == 0 && i + NS < nq && !abort_flag) verify_issue<FMT>(p, smem, full_bar, i + NS, q0, tpe, uexp);
+    if (tid < 128) {
+      const int col = tid >> 4, rl = tid & 15;
+      const int pair = pmap[u][col];
+      if (rl < rows && pair >= 0 && e >= 0 && e < p.E) {
+        float v = 0.f;
+#pragma unroll
+        for (int w = 0; w < KW; ++w) v += red[buf][w][rl * 8 + col];
+        if constexpr (FmtTraits<FMT>::kF16) v *= 64.f;
+        v = __bfloat162float(__float2bfloat16(v));
+        const int64_t o = static_cast<int64_t>(pair) * p.Nrows + n0 + rl;
+        if constexpr (PH == 1) {
+          const float r = fmaxf(v, 0.f);
+          static_cast<bf16*>(p.out)[o] = __float2bfloat16(r * r);
+        } else {
+          static_cast<float*>(p.out)[o] = v;
+        }
+      }
+    }
+  }
+  if (tid == 0 && abort_flag)
+    for (int i = max(0, nq - NS); i < nq; ++i) mbar_wait(smem_u32(&full_bar[i % NS]), (i / NS) & 1, kStatusDrainWait);
+}
+
+// out[t, n] = sum_k w[t, k] * part[t * topk + k, n] over the pairs whose expert is in
+// [e_begin, e_end) (fp32, k ascending); bf16 into `out` and/or fp32 into `out_f32`.
+__global__ void __launch_bounds__(256) moe_finalize_kernel(const float* __restrict__ part, const float* __restrict__ w,
+                                                           const int* __restrict__ idx, int R, int topk, int Nout,
+                                                           int e_begin, int e_end, bf16* __restrict__ out,
+                                                           float* __restrict__ out_f32) {
+  pdl_wait();
+  pdl_trigger();
+  const int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+  if (i >= static_cast<int64_t>(R) * Nout) return;
+  const int t = static_cast<int>(i / Nout), n = static_cast<int>(i % Nout);
+  float a = 0.f;
+  for (int k = 0; k < topk; ++k) {
+    const int pp = t * topk + k;
+    const int e = idx[pp];
+    if (e >= e_begin && e < e_end) a = fmaf(w[pp], part[static_cast<int64_t>(pp) * Nout + n], a);
+  }
+  if (out) out[i] = __float2bfloat16(a);
+  if (out_f32) out_f32[i] = a;
+}
+
+template <int FC, int TPR, int SPT>
+cudaError_t launch_seg(const SegParams& p, int grid, const LaunchCfg& cfg) {
+  auto kern = moe_seg_kernel<FC, TPR, SPT>;
+  const size_t smem = static_cast<size_t>(p.nstage) * p.stage_bytes;
+  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
+  if (e != cudaSuccess) return e;
+  return launch_kernel(kern, dim3(grid), dim3(kSegThreads), smem, cfg, p);
+}
+
+// threads per row: the candidate with the best lane utilisation (nslots / (TPR * SPT))
+template <int FC>
+cudaError_t dispatch_seg(SegParams& p, int grid, const LaunchCfg& cfg) {
+  const int nslots = p.K >> 4;
+  int best = 0;
+  double best_u = -1.0;
+  const int cand[4] = {256, 128, 64, 32};
+  for (int c : cand) {
+    const int spt = (nslots + c - 1) / c;
+    if (spt > 5) continue;
+    const double u = static_cast<double>(nslots) / (c * spt);
+    if (u > best_u + 1e-9) { best_u = u; best = c; }
+  }
+  const int spt = (nslots + best - 1) / best;
+  switch (best * 10 + spt) {
+    case 2561: return launch_seg<FC, 256, 1>(p, grid, cfg);
+    case 2562: return launch_seg<FC, 256, 2>(p, grid, cfg);
+    case 2563: return launch_seg<FC, 256, 3>(p, grid, cfg);
+    case 2564: return launch_seg<FC, 256, 4>(p, grid, cfg);
+    case 2565: return launch_seg<FC, 256, 5>(p, grid, cfg);
+    case 1281: return launch_seg<FC, 128, 1>(p, grid, cfg);
+    case 1282: return launch_seg<FC, 128, 2>(p, grid, cfg);
+    case 641: return launch_seg<FC, 64, 1>(p, grid, cfg);
+    case 642: return launch_seg<FC, 64, 2>(p, grid, cfg);
+    case 643: return launch_seg<FC, 64, 3>(p, grid, cfg);
+    case 321: return launch_seg<FC, 32, 1>(p, grid, cfg);
+    case 322: return launch_seg<FC, 32, 2>(p, grid, cfg);
+    case 323: return launch_seg<FC, 32, 3>(p, grid, cfg);
+    case 324: return launch_seg<FC, 32, 4>(p, grid, cfg);
+    case 325: return launch_seg<FC, 32, 5>(p, grid, cfg);
+    default: return cudaErrorInvalidValue;
+  }
+}
+
+template <int FMT, int PH, int KW, int CPW>
+cudaError_t launch_verify_ph(const VerifyParams& p, int grid, const LaunchCfg& cfg) {
+  auto kern = moe_verify_mma_kernel<FMT, PH, KW, CPW>;
+  const size_t smem = static_cast<size_t>(p.nstage) * p.stage_bytes;
+  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
+  if (e != cudaSuccess) return e;
+  return launch_kernel(kern, dim3(grid), dim3(KW * 32), smem, cfg, p);
+}
+
+template <int FMT, int PH>
+cudaError_t dispatch_verify_ph(const VerifyParams& p, int grid, const LaunchCfg& cfg) {
+  const int nchunks = p.K >> 6;
+  if (nchunks <= 16) return launch_verify_ph<FMT, PH, 8, 2>(p, grid, cfg);
+  if (nchunks <= 32) return launch_verify_ph<FMT, PH, 8, 4>(p, grid, cfg);
+  if (nchunks <= 40) return launch_verify_ph<FMT, PH, 8, 5>(p, grid, cfg);
+  if (nchunks <= 64) return launch_verify_ph<FMT, PH, 8, 8>(p, grid, cfg);
+  return launch_verify_ph<FMT, PH, 16, 8>(p, grid, cfg);
+}
+
+VerifyParams make_verify_params(int fmt, const bf16* xin, const int* meta, const uint8_t* wq, const bf16* sc, void* out,
+                                int P, int R, int E, int Nrows, int K, const LaunchCfg& cfg, int grid) {
+  VerifyParams p{xin, meta, wq, reinterpret_cast<const uint8_t*>(sc), out, P, R, E, Nrows, K, 0, 0, 0,
+                 cfg.early_weights ? 1 : 0};
+  const int64_t rb = fmt_row_bytes(fmt, K);
+  const int bpc = fmt == kFmtIq2N ? 16 : 32;
+  const uint32_t pad = static_cast<uint32_t>((bpc - rb % 128 + 128) % 128);
+  p.row_stride = static_cast<uint32_t>(rb) + pad;
+  const uint32_t scb = static_cast<uint32_t>(kTile * fmt_scale_row_bytes(fmt, K) + 32);
+  p.stage_bytes = (kTile * p.row_stride + scb + 127) & ~127u;
+  const int fit = static_cast<int>(cfg.smem_budget / p.stage_bytes);
+  p.nstage = std::max(2, std::min(fit, 16));
+  (void)grid;
+  return p;
+}
+
+}  // namespace
+
+cudaError_t launch_moe_route(const bf16* x, const bf16* gate_w, const float* bias, int R, int K, int E, int topk,
+                             float scale, int* idx, float* w, float* scores, const LaunchCfg& cfg) {
+  const unsigned blocks = static_cast<unsigned>((E + 3) / 4);
+  cudaError_t e = R <= 1 ? launch_kernel(router_logits_kernel<1>, dim3(blocks), dim3(128), 0, cfg, x, gate_w, R, K, E, scores)
+                         : launch_kernel(router_logits_kernel<8>, dim3(blocks), dim3(128), 0, cfg, x, gate_w, R, K, E, scores);
+  if (e != cudaSuccess) return e;
+  LaunchCfg c2 = cfg;
+  c2.pdl = true;  // same op: the selection waits for the logits with griddepcontrol.wait
+  return launch_kernel(router_topk_kernel, dim3(R), dim3(32), 0, c2, scores, bias, E, topk, scale, idx, w);
+}
+
+cudaError_t launch_moe_decode(const bf16* z, const int* idx, const float* w, const uint8_t* fc1_w, const bf16* fc1_s,
+                              const uint8_t* fc2_w, const bf16* fc2_s, int R, int E, int I, int topk, bf16* out,
+                              bf16* h, float* part, const LaunchCfg& cfg) {
+  const int P = R * topk;
+  const int grid1 = std::min(cfg.sms, std::max(1, I / kSegRows));
+  SegParams p1{z, idx, w, fc1_w, fc1_s, h, nullptr, nullptr, P, topk, E, I, 1024, 0, 0, cfg.early_weights ? 1 : 0};
+  p1.stage_bytes = (kSegRows * 512 + kSegRows * 64 + 32 + 127) & ~127u;
+  const int want1 = P * ((I / grid1 + kSegRows) / kSegRows + 1);
+  p1.nstage = std::max(2, std::min({want1, static_cast<int>(cfg.smem_budget / p1.stage_bytes), 16}));
+  cudaError_t e = dispatch_seg<1>(p1, grid1, cfg);
+  if (e != cudaSuccess) return e;
+  LaunchCfg c2 = cfg;
+  c2.pdl = true;
+  c2.early_weights = true;  // fc1 triggers only after its own wait: every input of this op is ready
+  const int grid2 = std::max(64, std::min(cfg.sms, 1024));  // <= 16 rows of every pair per CTA
+  SegParams p2{h, idx, w, fc2_w, fc2_s, nullptr, part, out, P, topk, E, 1024, I, 0, 0, 1};
+  p2.stage_bytes = static_cast<uint32_t>((kSegRows * (I / 2) + kSegRows * (I / 16) + 32 + 127) & ~127);
+  p2.nstage = std::max(2, std::min({P * 2, static_cast<int>(c2.smem_budget / p2.stage_bytes), 16}));
+  return dispatch_seg<2>(p2, grid2, c2);
+}
+
+cudaError_t launch_moe_verify(int fmt, const bf16* z, const int* idx, const float* w, const uint8_t* fc1_w,
+                              const bf16* fc1_s, const uint8_t* fc2_w, const bf16* fc2_s, int R, int E, int I,
+                              int topk, int e_begin, int e_end, bf16* out, bf16* h, float* part, int* meta,
+                              float* out_partial, const LaunchCfg& cfg) {
+  const int P = R * topk;
+  cudaError_t e = launch_kernel(moe_group_kernel, dim3(1), dim3(128), 0, cfg, idx, P, topk, e_begin, e_end, meta);
+  if (e != cudaSuccess) return e;
+  LaunchCfg c2 = cfg;
+  c2.pdl = true;
+  const int grid = cfg.sms;
+  VerifyParams p1 = make_verify_params(fmt, z, meta, fc1_w, fc1_s, h, P, R, E, I, 1024, c2, grid);
+  VerifyParams p2 = make_verify_params(fmt, h, meta, fc2_w, fc2_s, part, P, R, E, 1024, I, c2, grid);
+  switch (fmt) {
+    case kFmtQ4:
+      if ((e = dispatch_verify_ph<kFmtQ4, 1>(p1, grid, c2)) != cudaSuccess) return e;
+      if ((e = dispatch_verify_ph<kFmtQ4, 2>(p2, grid, c2)) != cudaSuccess) return e;
+      break;
+    case kFmtIq2Lut:
+      if ((e = dispatch_verify_ph<kFmtIq2Lut, 1>(p1, grid, c2)) != cudaSuccess) return e;
+      if ((e = dispatch_verify_ph<kFmtIq2Lut, 2>(p2, grid, c2)) != cudaSuccess) return e;
+      break;
+    default:
+      if ((e = dispatch_verify_ph<kFmtIq2N, 1>(p1, grid, c2)) != cudaSuccess) return e;
+      if ((e = dispatch_verify_ph<kFmtIq2N, 2>(p2, grid, c2)) != cudaSuccess) return e;
+      break;
+  }
+  const int64_t n = static_cast<int64_t>(R) * 1024;
+  return launch_kernel(moe_finalize_kernel, dim3(static_cast<unsigned>((n + 255) / 256)), dim3(256), 0, c2, part, w,
+                       idx, R, topk, 1024, e_begin, e_end, out, out_partial);
+}
+
+}  // namespace bolt

@@ -1,0 +1,178 @@
+"""The bolt ops on torch CUDA tensors -- a host-side mirror of the reference's ORT ops.
+
+Each function is one node of the reference's custom-op domain ``bolt`` (src/bolt_ops.cu:1469-1589):
+same name, inputs in the same order, same attributes, and outputs allocated in the shapes the
+reference's ``ComputeV2`` allocates.  The work runs on the current torch CUDA stream through
+libbolt_b200.so; there is no CPU path.  A failing shape check raises ``RuntimeError`` with the
+reference's message (the reference returns ORT_FAIL with the same text).
+"""
+from __future__ import annotations
+
+import ctypes
+
+import torch
+
+from ._lib import last_error, lib, shape_arg
+
+__all__ = ["Nvfp4Gemv", "Q8Gemv", "Q4Gemv", "MoeRoute", "MoeDecode", "MoeVerify", "moe_verify_shard",
+           "f32_to_bf16", "dequant", "set_launch_options", "device_status", "FMT_Q8", "FMT_Q4", "FMT_NVFP4",
+           "FMT_IQ2_LUT", "FMT_IQ2_NATIVE"]
+
+FMT_Q8, FMT_Q4, FMT_NVFP4, FMT_IQ2_LUT, FMT_IQ2_NATIVE = 0, 1, 2, 3, 4
+
+
+def _ptr(t):
+    return ctypes.c_void_p(t.data_ptr()) if t is not None else ctypes.c_void_p(0)
+
+
+def _stream(t):
+    return ctypes.c_void_p(torch.cuda.current_stream(t.device).cuda_stream)
+
+
+def _need(*tensors):
+    for t in tensors:
+        if not isinstance(t, torch.Tensor) or not t.is_cuda:
+            raise RuntimeError("bolt ops take CUDA tensors (there is no CPU implementation)")
+        if not t.is_contiguous():
+            raise RuntimeError("bolt ops take contiguous tensors")
+
+
+def _check(rc):
+    if rc != 0:
+        raise RuntimeError(last_error())
+
+
+def set_launch_options(pdl: bool = False, early_weights: bool = False, smem_budget: int = 0) -> None:
+    """Process-wide launch options (see bolt_set_launch_options in include/bolt_b200.h)."""
+    _check(lib().bolt_set_launch_options(int(pdl), int(early_weights), int(smem_budget)))
+
+
+def device_status() -> int:
+    """Read and clear the device status word of the current device (0 = no kernel gave up)."""
+    v = ctypes.c_uint(0)
+    _check(lib().bolt_get_device_status(ctypes.byref(v)))
+    return v.value
+
+
+def Nvfp4Gemv(x, w, w_scale, g):
+    """y[..., N] = bf16(g * x @ (e2m1 * e4m3)^T); w u8 [N, K/2], w_scale u8 [N, K/16], g f32 [1]."""
+    _need(x, w, w_scale, g)
+    y = torch.empty(*x.shape[:-1], w.shape[0], dtype=torch.bfloat16, device=x.device)
+    xs, _k1 = shape_arg(x.shape)
+    ws, _k2 = shape_arg(w.shape)
+    _check(lib().bolt_nvfp4_gemv(_ptr(x), xs, x.dim(), _ptr(w), ws, w.dim(), _ptr(w_scale), _ptr(g), _ptr(y),
+                                 _stream(x)))
+    return y
+
+
+def Q8Gemv(x, B, scales):
+    """y[..., N] = x @ W^T, W = (B - 128) * s; B u8 [N, K/32, 32], scales bf16 [N, K/32]."""
+    _need(x, B, scales)
+    y = torch.empty(*x.shape[:-1], B.shape[0], dtype=torch.bfloat16, device=x.device)
+    xs, _k1 = shape_arg(x.shape)
+    bs, _k2 = shape_arg(B.shape)
+    _check(lib().bolt_q8_gemv(_ptr(x), xs, x.dim(), _ptr(B), bs, B.dim(), _ptr(scales), _ptr(y), _stream(x)))
+    return y
+
+
+def Q4Gemv(x, B, scales, iq2: int = 0):
+    """int4 (iq2=0), IQ2_XXS LUT codes (iq2=1) or native IQ2_XXS records (iq2=2)."""
+    _need(x, B, scales)
+    y = torch.empty(*x.shape[:-1], B.shape[0], dtype=torch.bfloat16, device=x.device)
+    xs, _k1 = shape_arg(x.shape)
+    bs, _k2 = shape_arg(B.shape)
+    _check(lib().bolt_q4_gemv(_ptr(x), xs, x.dim(), _ptr(B), bs, B.dim(), _ptr(scales), int(iq2), _ptr(y),
+                              _stream(x)))
+    return y
+
+
+def MoeRoute(x, gate_w, bias, topk: int, scale: float):
+    """Returns (idx i32 [R, topk], w f32 [R, topk], scores f32 [R, E])."""
+    _need(x, gate_w, bias)
+    R, E = x.shape[0], gate_w.shape[0]
+    idx = torch.empty(R, topk, dtype=torch.int32, device=x.device)
+    w = torch.empty(R, topk, dtype=torch.float32, device=x.device)
+    scores = torch.empty(R, E, dtype=torch.float32, device=x.device)
+    xs, _k1 = shape_arg(x.shape)
+    gs, _k2 = shape_arg(gate_w.shape)
+    _check(lib().bolt_moe_route(_ptr(x), xs, x.dim(), _ptr(gate_w), gs, gate_w.dim(), _ptr(bias), int(topk),
+                                float(scale), _ptr(idx), _ptr(w), _ptr(scores), _stream(x)))
+    return idx, w, scores
+
+
+def _moe_outputs(z, fc1_w, topk):
+    R = z.shape[0]
+    I = fc1_w.shape[1]
+    P = R * topk
+    out = torch.empty(R, 1024, dtype=torch.bfloat16, device=z.device)
+    h = torch.empty(P, I, dtype=torch.bfloat16, device=z.device)
+    part = torch.empty(P, 1024, dtype=torch.float32, device=z.device)
+    return out, h, part
+
+
+def MoeDecode(z, idx, w, fc1_w, fc1_s, fc2_w, fc2_s, topk: int):
+    """Returns (out bf16 [R, 1024], h bf16 [R*topk, I], part f32 [R*topk, 1024])."""
+    _need(z, idx, w, fc1_w, fc1_s, fc2_w, fc2_s)
+    out, h, part = _moe_outputs(z, fc1_w, topk)
+    zs, _k1 = shape_arg(z.shape)
+    w1s, _k2 = shape_arg(fc1_w.shape)
+    _check(lib().bolt_moe_decode(_ptr(z), zs, z.dim(), _ptr(idx), _ptr(w), _ptr(fc1_w), w1s, fc1_w.dim(),
+                                 _ptr(fc1_s), _ptr(fc2_w), _ptr(fc2_s), int(topk), _ptr(out), _ptr(h), _ptr(part),
+                                 _stream(z)))
+    return out, h, part
+
+
+def MoeVerify(z, idx, w, fc1_w, fc1_s, fc2_w, fc2_s, topk: int, iq2: int = 0):
+    """Returns (out, h, part, meta i32 [1 + P + 8P])."""
+    _need(z, idx, w, fc1_w, fc1_s, fc2_w, fc2_s)
+    out, h, part = _moe_outputs(z, fc1_w, topk)
+    P = z.shape[0] * topk
+    meta = torch.empty(1 + P + 8 * P, dtype=torch.int32, device=z.device)
+    zs, _k1 = shape_arg(z.shape)
+    w1s, _k2 = shape_arg(fc1_w.shape)
+    _check(lib().bolt_moe_verify(_ptr(z), zs, z.dim(), _ptr(idx), _ptr(w), _ptr(fc1_w), w1s, fc1_w.dim(),
+                                 _ptr(fc1_s), _ptr(fc2_w), _ptr(fc2_s), int(topk), int(iq2), _ptr(out), _ptr(h),
+                                 _ptr(part), _ptr(meta), _stream(z)))
+    return out, h, part, meta
+
+
+def moe_verify_shard(z, idx, w, fc1_w, fc1_s, fc2_w, fc2_s, topk: int, iq2: int, e_begin: int, e_end: int,
+                     out_partial=None, outputs=None):
+    """MoeVerify over experts [e_begin, e_end) only; returns (out_partial f32 [R, 1024], h, part, meta).
+
+    ``fc1_w`` etc. hold the full [E, ...] tensors (or views of a full-size allocation whose
+    non-local experts are never read).
+    """
+    _need(z, idx, w, fc1_w, fc1_s, fc2_w, fc2_s)
+    R = z.shape[0]
+    P = R * topk
+    if outputs is None:
+        _, h, part = _moe_outputs(z, fc1_w, topk)
+        meta = torch.empty(1 + P + 8 * P, dtype=torch.int32, device=z.device)
+    else:
+        h, part, meta = outputs
+    if out_partial is None:
+        out_partial = torch.empty(R, 1024, dtype=torch.float32, device=z.device)
+    zs, _k1 = shape_arg(z.shape)
+    w1s, _k2 = shape_arg(fc1_w.shape)
+    _check(lib().bolt_moe_verify_shard(_ptr(z), zs, z.dim(), _ptr(idx), _ptr(w), _ptr(fc1_w), w1s, fc1_w.dim(),
+                                       _ptr(fc1_s), _ptr(fc2_w), _ptr(fc2_s), int(topk), int(iq2), int(e_begin),
+                                       int(e_end), ctypes.c_void_p(0), _ptr(h), _ptr(part), _ptr(meta),
+                                       _ptr(out_partial), _stream(z)))
+    return out_partial, h, part, meta
+
+
+def f32_to_bf16(t, out=None):
+    _need(t)
+    if out is None:
+        out = torch.empty(t.shape, dtype=torch.bfloat16, device=t.device)
+    _check(lib().bolt_f32_to_bf16(_ptr(t), _ptr(out), t.numel(), _stream(t)))
+    return out
+
+
+def dequant(fmt: int, w, scales, N: int, K: int, exact: bool = False):
+    """Weights [N, K] f32 decoded by the kernels' own decoders (contract checks)."""
+    _need(w, scales)
+    out = torch.empty(N, K, dtype=torch.float32, device=w.device)
+    _check(lib().bolt_dequant(int(fmt), int(exact), _ptr(w), _ptr(scales), int(N), int(K), _ptr(out), _stream(w)))
+    return out

@@ -116,7 +116,7 @@ def nvfp4_dequant(w: torch.Tensor, w_scale: torch.Tensor) -> torch.Tensor:
     w u8 [N, K/2] (two e2m1 per byte, low nibble first), w_scale u8 e4m3 bytes [N, K/16]
     (tests/test_bolt_ops.py:76-77; src/bolt_ops.cu:652-656,908-916).
     """
-    v = FP4_VALUES[unpack_nibbles(w).long()]
+    v = FP4_VALUES.to(w.device)[unpack_nibbles(w).long()]
     s = w_scale.contiguous().view(torch.float8_e4m3fn).to(torch.float32).repeat_interleave(16, dim=1)
     return v * s
 
@@ -129,7 +129,7 @@ def iq2_lut_dequant(B: torch.Tensor, scales: torch.Tensor) -> torch.Tensor:
     N = B.shape[0]
     nb = scales.shape[-1]
     codes = unpack_nibbles(B.reshape(N, nb, -1)).long()
-    v = IQ2_LUT_BF16[codes & 7]
+    v = IQ2_LUT_BF16.to(B.device)[codes & 7]
     return bf16_round(v * _scale_f32(scales).unsqueeze(-1)).reshape(N, -1)
 
 
@@ -154,7 +154,7 @@ def _iq2n_parts(B: torch.Tensor, D: torch.Tensor):
         parity ^= (signs7 >> b) & 1
     pattern = signs7 | (parity << 7)  # ggml ksigns: 8th sign = parity (src/bolt_ops.cu:827)
     bits = torch.stack([(pattern >> e) & 1 for e in range(8)], -1)  # [N, G, 4, 8]
-    mag = iq2xxs_grid()[gidx]  # [N, G, 4, 8]
+    mag = iq2xxs_grid().to(B.device)[gidx]  # [N, G, 4, 8]
     sign = 1.0 - 2.0 * bits.to(torch.float32)
     return db, mag, sign
 
@@ -238,6 +238,7 @@ def moe_route(x, gate_w, bias, topk: int, scale: float):
     scores = (1.0 / (1.0 + torch.exp(-logits))).to(torch.float32)
     R, E = scores.shape
     val = scores + bias.to(torch.float32).unsqueeze(0)
+    scores, val = scores.cpu(), val.cpu()
     idx = torch.full((R, topk), -1, dtype=torch.int32)
     wts = torch.zeros((R, topk), dtype=torch.float32)
     for r in range(R):
@@ -287,7 +288,7 @@ def moe_group_meta(idx: torch.Tensor, topk: int) -> torch.Tensor:
     pairs p = row * topk + k; [1+P + u*8 + row] = pair index p of row `row` for expert u,
     or -1.  The reference leaves slots [1+U, 1+P) unwritten; this contract sets them to -1.
     """
-    flat = idx.reshape(-1).tolist()
+    flat = idx.reshape(-1).cpu().tolist()
     P = len(flat)
     meta = torch.full((1 + P + 8 * P,), -1, dtype=torch.int32)
     uniq = []
@@ -321,9 +322,10 @@ def _moe_pairs(z, idx, w, fc1_w, fc1_s, fc2_w, fc2_s, topk, fmt, fp32=False):
     E = fc1_w.shape[0]
     P = R * topk
     acc_t = torch.float32 if fp32 else torch.float64
-    h = torch.zeros((P, I), dtype=torch.bfloat16)
-    part = torch.zeros((P, 1024), dtype=torch.float32)
-    flat = idx.reshape(-1)
+    dev = z.device
+    h = torch.zeros((P, I), dtype=torch.bfloat16, device=dev)
+    part = torch.zeros((P, 1024), dtype=torch.float32, device=dev)
+    flat = idx.reshape(-1).cpu()
     cache = {}
     for p in range(P):
         t = p // topk
@@ -331,6 +333,8 @@ def _moe_pairs(z, idx, w, fc1_w, fc1_s, fc2_w, fc2_s, topk, fmt, fp32=False):
         if e < 0 or e >= E:
             continue  # out-of-range expert ids contribute nothing (the reference reads out of bounds)
         if e not in cache:
+            if len(cache) >= 4:
+                cache.pop(next(iter(cache)))
             cache[e] = (moe_expert_weights(fc1_w, fc1_s, e, I, 1024, fmt).to(acc_t),
                         moe_expert_weights(fc2_w, fc2_s, e, 1024, I, fmt).to(acc_t))
         W1, W2 = cache[e]
