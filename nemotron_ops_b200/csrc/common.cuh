@@ -102,6 +102,23 @@ __device__ __forceinline__ void bulk_g2s(uint32_t dst, const void* src, uint32_t
       : "memory");
 }
 
+// Asks the bulk-copy engine to pull [p, p + bytes) into L2 (no destination, no completion).
+// p and bytes must be multiples of 16.
+__device__ __forceinline__ void prefetch_l2(const void* p, uint32_t bytes) {
+  asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(p), "r"(bytes) : "memory");
+}
+
+// L2 prefetch of the 16-byte aligned body of [p, p + len), in pieces of at most 1 MB.
+__device__ __forceinline__ void prefetch_span_l2(const void* p, uint64_t len) {
+  uintptr_t a = (reinterpret_cast<uintptr_t>(p) + 15) & ~uintptr_t(15);
+  const uintptr_t e = (reinterpret_cast<uintptr_t>(p) + len) & ~uintptr_t(15);
+  while (a < e) {
+    const uint32_t n = static_cast<uint32_t>(e - a < (1u << 20) ? e - a : (1u << 20));
+    prefetch_l2(reinterpret_cast<const void*>(a), n);
+    a += n;
+  }
+}
+
 // Stages the byte range [src, src + len) of a tensor whose valid bytes end at `end` into
 // shared memory so that byte src[i] lands at dst + (src & 15) + i.  The 16-byte aligned body
 // goes through the bulk-copy engine (its byte count is added to `tx`); the part beyond the

@@ -7,15 +7,16 @@
 // B200 design (not a translation of QGemvKernel):
 //  * persistent grid, one CTA per SM, each CTA owns a contiguous range of weight rows, so its
 //    weight bytes are one contiguous span of HBM;
-//  * 8-row stages (weights + the matching scale span) are streamed with cp.async.bulk into an
+//  * 16-row stages (weights + the matching scale span) are streamed with cp.async.bulk into an
 //    smem ring guarded by mbarriers; the whole per-CTA working set of the benchmark shapes is
 //    in flight from the first microsecond;
-//  * 8 warps compute: each thread owns 16-wide k slots of every row, keeps its x
+//  * 16 warps compute: each thread owns 16-wide k slots of every row, keeps its x
 //    slice in fp32 registers for the life of the CTA and dequantises with one prmt per weight
 //    into a float whose mantissa carries the code (Q4: 0.5 + n/256; Q8: 2^23 + b), feeding
 //    packed fma.rn.f32x2;
-//  * rows are reduced with a butterfly (reduce-scatter) over lanes and a double-buffered
-//    smem pass across warps; one named barrier per 8-row stage.
+//  * rows are reduced with a butterfly (reduce-scatter) over lanes; the cross-warp sum of a ring
+//    slot is done by the last warp to finish it, which also refills the slot -- there is no
+//    CTA-wide barrier in the main loop, so no warp waits for another.
 #include "common.cuh"
 #include "kernels.h"
 
@@ -23,9 +24,9 @@ namespace bolt {
 
 namespace {
 
-constexpr int kWarps = 8;
+constexpr int kWarps = 16;
 constexpr int kThreads = kWarps * 32;
-constexpr int kRowsPerStage = 8;
+constexpr int kRowsPerStage = 16;
 
 struct ExactParams {
   const bf16* x;
@@ -38,8 +39,6 @@ struct ExactParams {
   uint32_t stage_bytes;  // bytes of one ring slot (weights + scale span), multiple of 128
   int early_weights;     // stream weights before griddepcontrol.wait (weights are constants)
 };
-
-__device__ __forceinline__ void named_barrier_all() { asm volatile("bar.sync 1;" ::: "memory"); }
 
 // Reduce-scatter of NP per-row partials across the 32 lanes of a warp.  Afterwards every lane
 // holds the warp total of row (lane >> (5 - log2 NP)) & (NP - 1).
@@ -63,13 +62,15 @@ __device__ __forceinline__ float warp_reduce_rows(float (&v)[NP], int lane) {
 
 template <int NP>
 struct Log2 {
-  static constexpr int v = NP == 8 ? 3 : NP == 4 ? 2 : NP == 2 ? 1 : 0;
+  static constexpr int v = NP == 16 ? 4 : NP == 8 ? 3 : NP == 4 ? 2 : NP == 2 ? 1 : 0;
 };
 
-// Issues the bulk copies of stage `i` (8 rows + their scale span) into ring slot i % NS.
+// Issues the bulk copies of stage `i` (16 rows + their scale span) into ring slot i % NS.
+// Called by all lanes of one warp: lane 1 issues the weight copy, lane 0 the scale span and
+// the byte count (issuing a bulk copy costs a thread ~100 ns, so the two run side by side).
 template <int BITS>
 __device__ __forceinline__ void exact_issue_stage(const ExactParams& p, uint8_t* smem, uint64_t* full_bar, int i,
-                                                  int64_t r0, int nrows) {
+                                                  int64_t r0, int nrows, int lane) {
   const int nb = p.K >> 5;
   const uint32_t row_bytes = static_cast<uint32_t>(p.K) * BITS / 8;
   const int s = i % p.nstage;
@@ -79,22 +80,40 @@ __device__ __forceinline__ void exact_issue_stage(const ExactParams& p, uint8_t*
   const uint32_t fb = smem_u32(&full_bar[s]);
   const uint8_t* sc_bytes = reinterpret_cast<const uint8_t*>(p.sc);
   uint32_t tx = rows * row_bytes;
-  bulk_g2s(smem_u32(slot), p.w + row * row_bytes, rows * row_bytes, fb);
-  stage_span(slot + kRowsPerStage * row_bytes, sc_bytes + row * nb * 2, rows * nb * 2, sc_bytes + p.N * nb * 2, fb, tx);
-  mbar_arrive_expect_tx(fb, tx);
+  if (lane == 1) bulk_g2s(smem_u32(slot), p.w + row * row_bytes, rows * row_bytes, fb);
+  if (lane == 0) {
+    stage_span(slot + kRowsPerStage * row_bytes, sc_bytes + row * nb * 2, rows * nb * 2, sc_bytes + p.N * nb * 2, fb, tx);
+    mbar_arrive_expect_tx(fb, tx);
+  }
+  __syncwarp();
+}
+
+// Returns true in every lane of the warp that is the last of kWarps to finish ring slot `s`;
+// that warp then sees every other warp's partials (release / acquire through the counter).
+__device__ __forceinline__ bool last_warp_of_slot(int* cnt, int lane) {
+  __threadfence_block();
+  __syncwarp();
+  int last = 0;
+  if (lane == 0) last = atomicAdd(cnt, 1) == kWarps - 1;
+  last = __shfl_sync(0xffffffffu, last, 0);
+  if (last) __threadfence_block();
+  return last != 0;
 }
 
 // BITS: 4 or 8.  TPR: threads per row (256, 128 or 64).  SPT: 16-k slots per thread.
-// Thread 0 also issues the copies: it fills the ring up front and refills a slot right after
-// the per-stage barrier, which proves that every warp has finished reading it.
+// No CTA-wide barrier after the prologue: each warp writes the per-row partials of a ring slot
+// into red[slot], and the last warp to finish the slot sums them, writes those rows of y and
+// refills the slot with the stage NS ahead.
 template <int BITS, int TPR, int SPT>
 __global__ void __launch_bounds__(kThreads, 1) gemv_exact_kernel(const ExactParams p) {
   extern __shared__ __align__(128) uint8_t smem[];
   constexpr int RP = kThreads / TPR;         // rows processed side by side
   constexpr int NP = kRowsPerStage / RP;     // rows a thread touches per stage
+  constexpr int WPG = TPR / 32;              // warps per row group
   constexpr int SLOT_BYTES = BITS * 2;       // 16 weights
   __shared__ uint64_t full_bar[16];
-  __shared__ float red[2][kWarps][kRowsPerStage];
+  __shared__ int done_cnt[16];
+  __shared__ float red[16][kWarps][kRowsPerStage];
   __shared__ volatile int abort_flag;
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
@@ -108,15 +127,25 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_exact_kernel(const ExactPara
   const int NS = p.nstage;
 
   if (tid == 0) {
-    for (int s = 0; s < NS; ++s) mbar_init(smem_u32(&full_bar[s]), 1);
+    for (int s = 0; s < NS; ++s) {
+      mbar_init(smem_u32(&full_bar[s]), 1);
+      done_cnt[s] = 0;
+    }
     abort_flag = 0;
     fence_barrier_init();
   }
   __syncthreads();
   pdl_trigger();
-  if (tid == 0) {
-    if (!p.early_weights) pdl_wait();
-    for (int i = 0; i < min(NS, ntiles); ++i) exact_issue_stage<BITS>(p, smem, full_bar, i, r0, nrows);
+  if (warp == 0) {
+    if (p.early_weights) {
+      if (lane == 0) {
+        prefetch_span_l2(p.w + r0 * row_bytes, static_cast<uint64_t>(nrows) * row_bytes);
+        prefetch_span_l2(p.sc + r0 * nb, static_cast<uint64_t>(nrows) * nb * 2);
+      }
+    } else {
+      pdl_wait();
+    }
+    for (int i = 0; i < min(NS, ntiles); ++i) exact_issue_stage<BITS>(p, smem, full_bar, i, r0, nrows, lane);
   }
   pdl_wait();
 
@@ -229,24 +258,24 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_exact_kernel(const ExactPara
       part[u] = acc;
     }
 
-    // rows of this stage: warp-level reduce-scatter, then across the warps of the row group
+    // rows of this stage: warp-level reduce-scatter into red[s]; the last warp sums the warps
     const float v = warp_reduce_rows<NP>(part, lane);
     constexpr int kLanesPerRow = 32 / NP;
-    const int buf = i & 1;
     if ((lane & (kLanesPerRow - 1)) == 0) {
       const int li = (lane >> (5 - Log2<NP>::v)) & (NP - 1);
-      red[buf][warp][li * RP + rg] = v;
+      red[s][warp][li * RP + rg] = v;
     }
-    named_barrier_all();
-    if (tid == 0 && i + NS < ntiles && !abort_flag) exact_issue_stage<BITS>(p, smem, full_bar, i + NS, r0, nrows);
-    if (tid < rows) {
-      const int rl = tid;
-      const int grp = rl % RP;
-      constexpr int WPG = TPR / 32;  // warps per row group
-      float t = 0.f;
+    if (last_warp_of_slot(&done_cnt[s], lane)) {
+      if (lane < rows) {
+        const int grp = lane % RP;
+        float t = 0.f;
 #pragma unroll
-      for (int w = 0; w < WPG; ++w) t += red[buf][grp * WPG + w][rl];
-      p.y[row0 + rl] = __float2bfloat16(t);
+        for (int w = 0; w < WPG; ++w) t += red[s][grp * WPG + w][lane];
+        p.y[row0 + lane] = __float2bfloat16(t);
+      }
+      __syncwarp();
+      if (lane == 0) done_cnt[s] = 0;
+      if (i + NS < ntiles && !abort_flag) exact_issue_stage<BITS>(p, smem, full_bar, i + NS, r0, nrows, lane);
     }
   }
   if (tid == 0 && abort_flag)  // copies may still be landing: wait for them before exiting
@@ -333,7 +362,7 @@ cudaError_t launch_gemv_exact(int bits, const bf16* x, int R, const uint8_t* w, 
     const uint32_t row_bytes = static_cast<uint32_t>(K) * bits / 8;
     const uint32_t sc_bytes = kRowsPerStage * (K / 32) * 2 + 32;
     p.stage_bytes = (kRowsPerStage * row_bytes + sc_bytes + 127) & ~127u;
-    const int grid = static_cast<int>(std::min<int64_t>(cfg.sms, (N + kRowsPerStage - 1) / kRowsPerStage));
+    const int grid = static_cast<int>(std::min<int64_t>(cfg.sms, (N + 7) / 8));
     const int64_t rows_per_cta = (N + grid - 1) / grid;
     const int want = static_cast<int>((rows_per_cta + kRowsPerStage - 1) / kRowsPerStage);
     const int fit = static_cast<int>(cfg.smem_budget / p.stage_bytes);

@@ -21,7 +21,7 @@ struct LaunchCfg {
   int sms = 148;
   bool pdl = false;
   bool early_weights = false;
-  size_t smem_budget = 100 * 1024;  // ring bytes per CTA; ~half an SM so a PDL successor fits beside it
+  size_t smem_budget = 200 * 1024;  // staged bytes per CTA (one CTA per SM)
 };
 
 template <typename... KArgs, typename... Args>

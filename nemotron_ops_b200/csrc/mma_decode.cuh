@@ -21,6 +21,7 @@
 #include "common.cuh"
 #include "iq2xxs_grid.h"
 #include "kernels.h"
+#include "tensor_map.h"
 
 namespace bolt {
 
@@ -108,6 +109,63 @@ __device__ __forceinline__ RawRow load_raw(const uint8_t* row, const uint8_t* sc
   return r;
 }
 
+// Same as load_raw for a tile staged by a row_tile_map box: weights are swizzled; scales are
+// either swizzled the same way (sc_swz) or plain rows of sc_rb bytes.  c is the chunk index
+// inside the staged K range.
+// wsw: weight tile layout (1 = 128-byte swizzled pieces, 0 = 16-byte pieces).
+template <int FMT>
+__device__ __forceinline__ RawRow load_raw_swz(const uint8_t* wt, const uint8_t* st, bool sc_swz, int sc_rb, int r,
+                                               int c, int t, int wsw) {
+  RawRow o;
+  int sb;
+  if constexpr (FMT == kFmtQ8) {
+    o.w = *reinterpret_cast<const uint4*>(wt + tile_off(wsw, r, 64 * c + 16 * t));
+    sb = 2 * (2 * c + (t >> 1));
+  } else if constexpr (FMT == kFmtIq2N) {
+    const uint2 v = *reinterpret_cast<const uint2*>(wt + tile_off(wsw, r, 8 * (2 * c + (t >> 1))));
+    o.w = make_uint4(v.x, v.y, 0u, 0u);
+    sb = 2 * (c >> 2);
+  } else {
+    const uint2 v = *reinterpret_cast<const uint2*>(wt + tile_off(wsw, r, 32 * c + 8 * t));
+    o.w = make_uint4(v.x, v.y, 0u, 0u);
+    sb = FMT == kFmtFp4 ? 4 * c + t : 2 * (2 * c + (t >> 1));
+  }
+  const uint8_t* sp = sc_swz ? st + swz_off(r, sb) : st + r * sc_rb + sb;
+  o.s = FMT == kFmtFp4 ? static_cast<uint32_t>(*sp) : static_cast<uint32_t>(*reinterpret_cast<const uint16_t*>(sp));
+  return o;
+}
+
+// Byte offset (row-relative layout) of this thread's weights for stage-local chunk c: the
+// kernels precompute tile offsets from it once per CTA.
+template <int FMT>
+__host__ __device__ __forceinline__ int chunk_byte(int c, int t) {
+  if (FMT == kFmtQ8) return 64 * c + 16 * t;
+  if (FMT == kFmtIq2N) return 8 * (2 * c + (t >> 1));
+  return 32 * c + 8 * t;
+}
+// Byte offset of this thread's scale for stage-local chunk c inside the row's scales.
+template <int FMT>
+__host__ __device__ __forceinline__ int chunk_scale_byte(int c, int t) {
+  if (FMT == kFmtFp4) return 4 * c + t;
+  if (FMT == kFmtIq2N) return 2 * (c >> 2);
+  return 2 * (2 * c + (t >> 1));
+}
+
+template <int FMT>
+__device__ __forceinline__ uint4 load_w_at(const uint8_t* p) {
+  if constexpr (FMT == kFmtQ8) {
+    return *reinterpret_cast<const uint4*>(p);
+  } else {
+    const uint2 v = *reinterpret_cast<const uint2*>(p);
+    return make_uint4(v.x, v.y, 0u, 0u);
+  }
+}
+template <int FMT>
+__device__ __forceinline__ uint32_t load_s_at(const uint8_t* p) {
+  if constexpr (FMT == kFmtFp4) return static_cast<uint32_t>(*p);
+  else return static_cast<uint32_t>(*reinterpret_cast<const uint16_t*>(p));
+}
+
 // IQ2 LUT byte planes: bf16 of {8, 25, 43, 0} (codes 0..3) and their negatives (codes 4..7)
 constexpr uint32_t kLutHiPos = 0x00424141u, kLutHiNeg = 0x00C2C1C1u;
 constexpr uint32_t kLutLoPos = 0x002CC800u, kLutLoNeg = 0x002CC800u;
@@ -192,6 +250,32 @@ __device__ __forceinline__ void decode_row(const RawRow& r, int t, const uint32_
   }
 }
 
+// Raw (unscaled) decode for the block-column mode of R = 1 exact-weight GEMVs: the block
+// scales are applied to the MMA results instead.
+//   Q4:    bf16 (128 + n), PERM pairs -- the constant 136 is removed with the block sums of x
+//   NVFP4: fp16 e2m1 values (exact), ADJ pairs
+template <int FMT>
+__device__ __forceinline__ void decode_row_raw(const RawRow& r, uint32_t (&out)[8]) {
+  if constexpr (FMT == kFmtQ4) {
+#pragma unroll
+    for (int s = 0; s < 4; ++s) {
+      out[2 * s] = ((r.w.x >> (4 * s)) & 0x000F000Fu) | 0x43004300u;
+      out[2 * s + 1] = ((r.w.y >> (4 * s)) & 0x000F000Fu) | 0x43004300u;
+    }
+  } else {
+    static_assert(FMT == kFmtFp4, "block-column mode exists for Q4 and NVFP4");
+    asm("{\n .reg .b8 b0, b1, b2, b3, b4, b5, b6, b7;\n"
+        " mov.b32 {b0, b1, b2, b3}, %8;\n mov.b32 {b4, b5, b6, b7}, %9;\n"
+        " cvt.rn.f16x2.e2m1x2 %0, b0;\n cvt.rn.f16x2.e2m1x2 %1, b1;\n"
+        " cvt.rn.f16x2.e2m1x2 %2, b2;\n cvt.rn.f16x2.e2m1x2 %3, b3;\n"
+        " cvt.rn.f16x2.e2m1x2 %4, b4;\n cvt.rn.f16x2.e2m1x2 %5, b5;\n"
+        " cvt.rn.f16x2.e2m1x2 %6, b6;\n cvt.rn.f16x2.e2m1x2 %7, b7;\n}\n"
+        : "=r"(out[0]), "=r"(out[1]), "=r"(out[2]), "=r"(out[3]), "=r"(out[4]), "=r"(out[5]), "=r"(out[6]),
+          "=r"(out[7])
+        : "r"(r.w.x), "r"(r.w.y));
+  }
+}
+
 // ---------------------------------------------------------------------------------------
 // activation (B) fragments
 // ---------------------------------------------------------------------------------------
@@ -234,6 +318,21 @@ __device__ __forceinline__ void mma16816(float (&c)[4], uint32_t a0, uint32_t a1
                  : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
                  : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
   }
+}
+
+// One chunk of a swizzled 16-row tile: decode rows g and g+8, four MMAs.
+template <int FMT>
+__device__ __forceinline__ void mma_chunk_swz(const uint8_t* wt, const uint8_t* st, bool sc_swz, int sc_rb, int g, int c,
+                                              int t, int wsw, const uint32_t* grid, const uint32_t (&b)[8],
+                                              float (&acc)[4]) {
+  const RawRow ra = load_raw_swz<FMT>(wt, st, sc_swz, sc_rb, g, c, t, wsw);
+  const RawRow rb = load_raw_swz<FMT>(wt, st, sc_swz, sc_rb, g + 8, c, t, wsw);
+  uint32_t da[8], db[8];
+  decode_row<FMT>(ra, t, grid, da);
+  decode_row<FMT>(rb, t, grid, db);
+#pragma unroll
+  for (int s = 0; s < 4; ++s)
+    mma16816<FmtTraits<FMT>::kF16>(acc, da[2 * s], db[2 * s], da[2 * s + 1], db[2 * s + 1], b[2 * s], b[2 * s + 1]);
 }
 
 // One chunk of one 16-row tile: decode rows g and g+8, four MMAs.

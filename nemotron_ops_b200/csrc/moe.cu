@@ -458,7 +458,7 @@ template <int FMT, int PH, int KW, int CPW>
 __global__ void __launch_bounds__(KW * 32, 1) moe_verify_mma_kernel(const VerifyParams p) {
   extern __shared__ __align__(128) uint8_t smem[];
   __shared__ uint64_t full_bar[16];
-  __shared__ float red[2][KW][128];
+  __shared__ __align__(16) float red[2][KW][128];
   __shared__ __align__(16) uint32_t grid_s[(FMT == kFmtIq2N) ? 1024 : 4];
   __shared__ int uexp[kMaxPairs];
   __shared__ int pmap[kMaxPairs][8];
