@@ -39,7 +39,7 @@ __all__ = [
     "FP4_VALUES", "IQ2_LUT_BF16", "iq2xxs_grid", "bf16_round", "unpack_nibbles",
     "q8_dequant", "q4_dequant", "nvfp4_dequant", "iq2_lut_dequant", "iq2n_dequant",
     "iq2n_dequant_gguf_style", "gemv_contract", "q8_gemv", "q4_gemv", "nvfp4_gemv",
-    "moe_route", "route_min_gap", "moe_group_meta", "moe_decode", "moe_verify",
+    "moe_route", "route_min_gap", "moe_group_meta", "moe_decode", "moe_verify", "moe_combine",
     "moe_expert_weights",
 ]
 
@@ -316,7 +316,10 @@ def moe_expert_weights(fc_w, fc_s, e: int, n_out: int, k_in: int, fmt: str):
     raise ValueError(fmt)
 
 
-def _moe_pairs(z, idx, w, fc1_w, fc1_s, fc2_w, fc2_s, topk, fmt, fp32=False):
+def _moe_pairs(z, idx, w, fc1_w, fc1_s, fc2_w, fc2_s, topk, fmt, fp32=False, h_in=None):
+    """h_in: stage-wise checking -- take the fc1 output h [P, I] from the caller instead of
+    computing it, so the fc2 stage can be compared against a reference that shares its input
+    exactly with the kernel under test."""
     R = z.shape[0]
     I = fc1_w.shape[1]
     E = fc1_w.shape[0]
@@ -338,9 +341,12 @@ def _moe_pairs(z, idx, w, fc1_w, fc1_s, fc2_w, fc2_s, topk, fmt, fp32=False):
             cache[e] = (moe_expert_weights(fc1_w, fc1_s, e, I, 1024, fmt).to(acc_t),
                         moe_expert_weights(fc2_w, fc2_s, e, 1024, I, fmt).to(acc_t))
         W1, W2 = cache[e]
-        a = bf16_round((z[t].to(acc_t) @ W1.T).to(torch.float32))  # bf16(z . W1) (:519, :1159)
-        r = torch.clamp(a, min=0.0)
-        h[p] = (r * r).to(torch.bfloat16)  # bf16(relu^2), r*r exact in fp32 (:520, :1162)
+        if h_in is None:
+            a = bf16_round((z[t].to(acc_t) @ W1.T).to(torch.float32))  # bf16(z . W1) (:519, :1159)
+            r = torch.clamp(a, min=0.0)
+            h[p] = (r * r).to(torch.bfloat16)  # bf16(relu^2), r*r exact in fp32 (:520, :1162)
+        else:
+            h[p] = h_in[p].to(device=dev, dtype=torch.bfloat16)
         part[p] = bf16_round((h[p].to(acc_t) @ W2.T).to(torch.float32))  # float(bf16(h . W2)) (:549, :1164)
     wt = w.reshape(R, topk).to(acc_t)
     pr = part.reshape(R, topk, 1024).to(acc_t)
@@ -348,13 +354,21 @@ def _moe_pairs(z, idx, w, fc1_w, fc1_s, fc2_w, fc2_s, topk, fmt, fp32=False):
     return out, h, part
 
 
-def moe_decode(z, idx, w, fc1_w, fc1_s, fc2_w, fc2_s, topk: int, fp32: bool = False):
+def moe_decode(z, idx, w, fc1_w, fc1_s, fc2_w, fc2_s, topk: int, fp32: bool = False, h_in=None):
     """MoeDecode (src/bolt_ops.cu:474-619): int4 experts with the exact fp32 weight contract."""
-    return _moe_pairs(z, idx, w, fc1_w, fc1_s, fc2_w, fc2_s, topk, "q4_exact", fp32)
+    return _moe_pairs(z, idx, w, fc1_w, fc1_s, fc2_w, fc2_s, topk, "q4_exact", fp32, h_in=h_in)
 
 
-def moe_verify(z, idx, w, fc1_w, fc1_s, fc2_w, fc2_s, topk: int, iq2: int = 0, fp32: bool = False):
+def moe_verify(z, idx, w, fc1_w, fc1_s, fc2_w, fc2_s, topk: int, iq2: int = 0, fp32: bool = False, h_in=None):
     """MoeVerify (src/bolt_ops.cu:1078-1257): bf16-rounded (tensor-core) weight contract."""
     fmt = {0: "q4_mma", 1: "iq2_lut", 2: "iq2n"}[iq2]
-    out, h, part = _moe_pairs(z, idx, w, fc1_w, fc1_s, fc2_w, fc2_s, topk, fmt, fp32)
+    out, h, part = _moe_pairs(z, idx, w, fc1_w, fc1_s, fc2_w, fc2_s, topk, fmt, fp32, h_in=h_in)
     return out, h, part, moe_group_meta(idx, topk)
+
+
+def moe_combine(part: torch.Tensor, w: torch.Tensor, topk: int) -> torch.Tensor:
+    """out[r] = bf16(sum_k w[r, k] * part[r * topk + k]) (src/bolt_ops.cu:552-587), fp64 sum."""
+    R = w.numel() // topk
+    pr = part.reshape(R, topk, 1024).to(torch.float64)
+    wt = w.reshape(R, topk).to(device=part.device, dtype=torch.float64)
+    return (wt.unsqueeze(-1) * pr).sum(1).to(torch.float32).to(torch.bfloat16)

@@ -74,19 +74,30 @@ def test_route_topk_above_expert_count():
 # ---------------------------------------------------------------------------------------------
 # MoeDecode / MoeVerify
 # ---------------------------------------------------------------------------------------------
-def _check_moe(op, ins, topk, iq2=0, check_h=True):
+# The MoE epilogues round twice before fc2 (a = bf16(z . W1), h = bf16(relu(a)^2)), so h may
+# differ from the fp64 oracle by up to ~1.2% where either rounding flips; such a flip then
+# moves fc2's partial sums by far more than 1e-3 where they cancel.  Each stage is therefore
+# checked against the oracle fed with the kernel's own input of that stage, and the end-to-end
+# output with the reference tests' own relative-norm criterion (tests/test_bolt_ops.py:63-65).
+H_RTOL = 1.6e-2  # two bf16 roundings (2^-8 each, the first one doubled by the square)
+
+
+def _check_moe(op, ins, topk, iq2=0, on_device=False):
     dev = _dev(ins)
+    src = dev if on_device else ins
     if op == "MoeDecode":
         out, h, part = ops.MoeDecode(*dev, topk=topk)
-        oo, oh, op_ = O.moe_decode(*ins, topk=topk)
+        oo, oh, op_ = O.moe_decode(*src, topk=topk)
+        _, _, op2 = O.moe_decode(*src, topk=topk, h_in=h.to(src[0].device))
     else:
         out, h, part, meta = ops.MoeVerify(*dev, topk=topk, iq2=iq2)
-        oo, oh, op_, om = O.moe_verify(*ins, topk=topk, iq2=iq2)
+        oo, oh, op_, om = O.moe_verify(*src, topk=topk, iq2=iq2)
+        _, _, op2, _ = O.moe_verify(*src, topk=topk, iq2=iq2, h_in=h.to(src[0].device))
         assert torch.equal(meta.cpu(), om)
-    if check_h:
-        assert_close(h, oh)
-        assert_close(part, op_)
-    assert_close(out, oo)
+    assert_close(h, oh, rtol=H_RTOL)                            # fc1 + relu^2
+    assert_close(part, op2)                                     # fc2 from the kernel's h
+    assert_close(out, O.moe_combine(part.to(src[0].device), src[2], topk))  # weighted sum
+    assert rel(out, oo) < 1e-2                                  # end to end
     assert ops.device_status() == 0
     return out
 
@@ -118,14 +129,8 @@ def test_moe_verify_config_r8(iq2):
     idx, w = _routed(8, 304, 8, 3)
     ex = W.moe_experts(E=304, I=2304, iq2=iq2)
     z = W.moe_latent(R=8)
-    dev = [z, idx, w, ex["fc1_w"], ex["fc1_s"], ex["fc2_w"], ex["fc2_s"]]
-    out, h, part, meta = ops.MoeVerify(*dev, topk=8, iq2=iq2)
     # fp64 oracle run on the GPU tensors (the oracle is device-agnostic torch)
-    oo, oh, op_, om = O.moe_verify(*dev, topk=8, iq2=iq2)
-    assert torch.equal(meta.cpu(), om)
-    assert_close(h, oh)
-    assert_close(part, op_)
-    assert_close(out, oo)
+    _check_moe("MoeVerify", [z, idx, w, ex["fc1_w"], ex["fc1_s"], ex["fc2_w"], ex["fc2_s"]], 8, iq2, on_device=True)
 
 
 @pytest.mark.parametrize("R,E,I,topk", [(2, 24, 256, 3), (5, 40, 512, 4), (8, 12, 256, 6), (8, 64, 768, 8)])
@@ -163,7 +168,8 @@ def test_moe_decode_skips_out_of_range_expert():
     ins = [z, idx, w] + [ex[k].cpu() for k in ("fc1_w", "fc1_s", "fc2_w", "fc2_s")]
     out, h, part = ops.MoeDecode(*_dev(ins), topk=topk)
     oo, oh, op_ = O.moe_decode(*ins, topk=topk)
-    assert_close(out, oo)
+    assert_close(h, oh, rtol=H_RTOL)
+    assert rel(out, oo) < 1e-2
     assert float(h[1:].abs().max()) == 0.0 and float(part[1:].abs().max()) == 0.0
 
 
