@@ -63,8 +63,10 @@ BOLT_API int bolt_set_launch_options(int pdl, int early_weights, int64_t smem_bu
 
 /*
  * Reads and clears the device status word of the current device (synchronises the device).
- * Nonzero bits mean a kernel gave up a bounded wait (2 s) and returned without finishing;
- * bit 3 means a MoE expert id outside [0, E) was skipped.  No counterpart in the reference.
+ * Nonzero bits mean a kernel gave up a bounded wait (2 s) and returned without finishing
+ * (bits 0-2, 4); bit 3 means a MoE expert id outside [0, E) was skipped; bit 5 means a
+ * kernel found its shared-memory carve-out misaligned and returned without computing.
+ * No counterpart in the reference.
  */
 BOLT_API int bolt_get_device_status(unsigned* status);
 

@@ -228,8 +228,8 @@ static int qgemv(int bits, const void* x, const int64_t* x_shape, int x_rank, co
       e = launch_gemv_mma(kFmtIq2N, xb, static_cast<int>(R), wb, scales, nullptr, N, static_cast<int>(K), yb, cfg);
     } else if (iq2) {
       e = launch_gemv_mma(kFmtIq2Lut, xb, static_cast<int>(R), wb, scales, nullptr, N, static_cast<int>(K), yb, cfg);
-    } else if ((R >= 2 || bits == 4) && K % 64 == 0 && K <= 8192 && aligned16(x) && aligned16(B) &&
-               aligned16(scales)) {
+    } else if ((R >= 2 || (bits == 4 && K % 256 == 0)) && K % 64 == 0 && K <= 8192 && aligned16(x) &&
+               aligned16(B) && aligned16(scales)) {
       // 2..8 rows: tensor-core contract; Q4 at R = 1: exact contract in block-column mode
       e = launch_gemv_mma(bits == 8 ? kFmtQ8 : kFmtQ4, xb, static_cast<int>(R), wb, scales, nullptr, N,
                           static_cast<int>(K), yb, cfg);

@@ -29,6 +29,7 @@ enum StatusBits : unsigned {
   kStatusDrainWait = 1u << 2,   // exit drain of in-flight copies timed out
   kStatusBadExpert = 1u << 3,   // an expert id outside [0, E) was skipped
   kStatusGridWait = 1u << 4,    // a cross-CTA wait timed out
+  kStatusSmemAlign = 1u << 5,   // the shared-memory carve-out was not aligned as required
 };
 
 extern __device__ unsigned g_status;
@@ -149,6 +150,15 @@ __device__ __forceinline__ uint32_t stage_span(uint8_t* dst, const uint8_t* src,
 __device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
 // Lets the next grid in the stream (launched with the PDL attribute) start its prologue.
 __device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;"); }
+
+// Named barrier `id` (1..15) over the first `threads` threads of the block (a multiple of 32);
+// barrier 0 is __syncthreads.
+__device__ __forceinline__ void named_bar_sync(int id, int threads) {
+  asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(threads) : "memory");
+}
+
+// 16-byte shared-memory load
+__device__ __forceinline__ uint4 lds128(const void* p) { return *reinterpret_cast<const uint4*>(p); }
 
 // ---------------------------------------------------------------------------------------
 // arithmetic helpers

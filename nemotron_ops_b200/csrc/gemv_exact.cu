@@ -365,7 +365,7 @@ cudaError_t launch_gemv_exact(int bits, const bf16* x, int R, const uint8_t* w, 
     const int grid = static_cast<int>(std::min<int64_t>(cfg.sms, (N + 7) / 8));
     const int64_t rows_per_cta = (N + grid - 1) / grid;
     const int want = static_cast<int>((rows_per_cta + kRowsPerStage - 1) / kRowsPerStage);
-    const int fit = static_cast<int>(cfg.smem_budget / p.stage_bytes);
+    const int fit = static_cast<int>((cfg.smem_budget ? cfg.smem_budget : 200 * 1024) / p.stage_bytes);
     p.nstage = std::max(2, std::min({want, fit, 16}));
     return bits == 8 ? dispatch_stream<8>(p, grid, cfg) : dispatch_stream<4>(p, grid, cfg);
   }

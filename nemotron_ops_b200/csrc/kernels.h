@@ -21,7 +21,9 @@ struct LaunchCfg {
   int sms = 148;
   bool pdl = false;
   bool early_weights = false;
-  size_t smem_budget = 200 * 1024;  // staged bytes per CTA (one CTA per SM)
+  // staged bytes per CTA; 0 = the kernel family's default (the tensor-core GEMV keeps two CTAs
+  // per SM so a PDL successor can stream while this call computes; the others use one)
+  size_t smem_budget = 0;
 };
 
 template <typename... KArgs, typename... Args>

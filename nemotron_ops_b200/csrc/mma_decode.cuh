@@ -109,32 +109,6 @@ __device__ __forceinline__ RawRow load_raw(const uint8_t* row, const uint8_t* sc
   return r;
 }
 
-// Same as load_raw for a tile staged by a row_tile_map box: weights are swizzled; scales are
-// either swizzled the same way (sc_swz) or plain rows of sc_rb bytes.  c is the chunk index
-// inside the staged K range.
-// wsw: weight tile layout (1 = 128-byte swizzled pieces, 0 = 16-byte pieces).
-template <int FMT>
-__device__ __forceinline__ RawRow load_raw_swz(const uint8_t* wt, const uint8_t* st, bool sc_swz, int sc_rb, int r,
-                                               int c, int t, int wsw) {
-  RawRow o;
-  int sb;
-  if constexpr (FMT == kFmtQ8) {
-    o.w = *reinterpret_cast<const uint4*>(wt + tile_off(wsw, r, 64 * c + 16 * t));
-    sb = 2 * (2 * c + (t >> 1));
-  } else if constexpr (FMT == kFmtIq2N) {
-    const uint2 v = *reinterpret_cast<const uint2*>(wt + tile_off(wsw, r, 8 * (2 * c + (t >> 1))));
-    o.w = make_uint4(v.x, v.y, 0u, 0u);
-    sb = 2 * (c >> 2);
-  } else {
-    const uint2 v = *reinterpret_cast<const uint2*>(wt + tile_off(wsw, r, 32 * c + 8 * t));
-    o.w = make_uint4(v.x, v.y, 0u, 0u);
-    sb = FMT == kFmtFp4 ? 4 * c + t : 2 * (2 * c + (t >> 1));
-  }
-  const uint8_t* sp = sc_swz ? st + swz_off(r, sb) : st + r * sc_rb + sb;
-  o.s = FMT == kFmtFp4 ? static_cast<uint32_t>(*sp) : static_cast<uint32_t>(*reinterpret_cast<const uint16_t*>(sp));
-  return o;
-}
-
 // Byte offset (row-relative layout) of this thread's weights for stage-local chunk c: the
 // kernels precompute tile offsets from it once per CTA.
 template <int FMT>
@@ -306,6 +280,45 @@ __device__ __forceinline__ void make_b_frags(const uint32_t (&x16)[8], uint32_t 
   }
 }
 
+// Shared-memory B-fragment layout of the streaming kernels: an activation row is kept as
+// 16-byte pieces (8 consecutive k); a lane's chunk operand is two pieces.  Converting a piece in
+// place needs no other piece, so the conversion pass reads and writes conflict-free.
+//   PERM (Q4, Q8): piece 0 of a lane's 16 k becomes (b0, b2, b4, b6), piece 1 (b1, b3, b5, b7);
+//   fp16 (NVFP4): each bf16 pair becomes fp16 of x * 2^-6, in place;
+//   ADJ bf16 (IQ2 LUT, native IQ2_XXS): the raw bf16 pairs are the operand.
+template <int FMT>
+__device__ __forceinline__ uint4 x_piece_to_frag(uint4 v) {
+  if constexpr (FmtTraits<FMT>::kXLayout == kXPerm) {
+    return make_uint4(prmt(v.x, v.z, 0x5410u), prmt(v.x, v.z, 0x7632u), prmt(v.y, v.w, 0x5410u),
+                      prmt(v.y, v.w, 0x7632u));
+  } else if constexpr (FmtTraits<FMT>::kF16) {
+    const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+    uint32_t o[4];
+#pragma unroll
+    for (int i = 0; i < 4; ++i)
+      o[i] = h2_bits(__floats2half2_rn(__uint_as_float(w[i] << 16) * 0.015625f,
+                                       __uint_as_float(w[i] & 0xFFFF0000u) * 0.015625f));
+    return make_uint4(o[0], o[1], o[2], o[3]);
+  } else {
+    return v;
+  }
+}
+template <int FMT>
+__host__ __device__ constexpr bool x_needs_conversion() {
+  return FmtTraits<FMT>::kXLayout == kXPerm || FmtTraits<FMT>::kF16;
+}
+// The 8 B registers of one chunk from its two converted pieces.
+template <int FMT>
+__device__ __forceinline__ void frag_from_pieces(uint4 p0, uint4 p1, uint32_t (&b)[8]) {
+  if constexpr (FmtTraits<FMT>::kXLayout == kXPerm) {
+    b[0] = p0.x; b[1] = p1.x; b[2] = p0.y; b[3] = p1.y;
+    b[4] = p0.z; b[5] = p1.z; b[6] = p0.w; b[7] = p1.w;
+  } else {
+    b[0] = p0.x; b[1] = p0.y; b[2] = p0.z; b[3] = p0.w;
+    b[4] = p1.x; b[5] = p1.y; b[6] = p1.z; b[7] = p1.w;
+  }
+}
+
 template <bool F16>
 __device__ __forceinline__ void mma16816(float (&c)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
                                          uint32_t b0, uint32_t b1) {
@@ -318,21 +331,6 @@ __device__ __forceinline__ void mma16816(float (&c)[4], uint32_t a0, uint32_t a1
                  : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
                  : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
   }
-}
-
-// One chunk of a swizzled 16-row tile: decode rows g and g+8, four MMAs.
-template <int FMT>
-__device__ __forceinline__ void mma_chunk_swz(const uint8_t* wt, const uint8_t* st, bool sc_swz, int sc_rb, int g, int c,
-                                              int t, int wsw, const uint32_t* grid, const uint32_t (&b)[8],
-                                              float (&acc)[4]) {
-  const RawRow ra = load_raw_swz<FMT>(wt, st, sc_swz, sc_rb, g, c, t, wsw);
-  const RawRow rb = load_raw_swz<FMT>(wt, st, sc_swz, sc_rb, g + 8, c, t, wsw);
-  uint32_t da[8], db[8];
-  decode_row<FMT>(ra, t, grid, da);
-  decode_row<FMT>(rb, t, grid, db);
-#pragma unroll
-  for (int s = 0; s < 4; ++s)
-    mma16816<FmtTraits<FMT>::kF16>(acc, da[2 * s], db[2 * s], da[2 * s + 1], db[2 * s + 1], b[2 * s], b[2 * s + 1]);
 }
 
 // One chunk of one 16-row tile: decode rows g and g+8, four MMAs.

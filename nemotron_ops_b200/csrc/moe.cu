@@ -671,7 +671,7 @@ VerifyParams make_verify_params(int fmt, const bf16* xin, const int* meta, const
   p.row_stride = static_cast<uint32_t>(rb) + pad;
   const uint32_t scb = static_cast<uint32_t>(kTile * fmt_scale_row_bytes(fmt, K) + 32);
   p.stage_bytes = (kTile * p.row_stride + scb + 127) & ~127u;
-  const int fit = static_cast<int>(cfg.smem_budget / p.stage_bytes);
+  const int fit = static_cast<int>((cfg.smem_budget ? cfg.smem_budget : 200 * 1024) / p.stage_bytes);
   p.nstage = std::max(2, std::min(fit, 16));
   (void)grid;
   return p;
@@ -698,7 +698,7 @@ cudaError_t launch_moe_decode(const bf16* z, const int* idx, const float* w, con
   SegParams p1{z, idx, w, fc1_w, fc1_s, h, nullptr, nullptr, P, topk, E, I, 1024, 0, 0, cfg.early_weights ? 1 : 0};
   p1.stage_bytes = (kSegRows * 512 + kSegRows * 64 + 32 + 127) & ~127u;
   const int want1 = P * ((I / grid1 + kSegRows) / kSegRows + 1);
-  p1.nstage = std::max(2, std::min({want1, static_cast<int>(cfg.smem_budget / p1.stage_bytes), 16}));
+  p1.nstage = std::max(2, std::min({want1, static_cast<int>((cfg.smem_budget ? cfg.smem_budget : 200 * 1024) / p1.stage_bytes), 16}));
   cudaError_t e = dispatch_seg<1>(p1, grid1, cfg);
   if (e != cudaSuccess) return e;
   LaunchCfg c2 = cfg;
@@ -707,7 +707,7 @@ cudaError_t launch_moe_decode(const bf16* z, const int* idx, const float* w, con
   const int grid2 = std::max(64, std::min(cfg.sms, 1024));  // <= 16 rows of every pair per CTA
   SegParams p2{h, idx, w, fc2_w, fc2_s, nullptr, part, out, P, topk, E, 1024, I, 0, 0, 1};
   p2.stage_bytes = static_cast<uint32_t>((kSegRows * (I / 2) + kSegRows * (I / 16) + 32 + 127) & ~127);
-  p2.nstage = std::max(2, std::min({P * 2, static_cast<int>(c2.smem_budget / p2.stage_bytes), 16}));
+  p2.nstage = std::max(2, std::min({P * 2, static_cast<int>((c2.smem_budget ? c2.smem_budget : 200 * 1024) / p2.stage_bytes), 16}));
   return dispatch_seg<2>(p2, grid2, c2);
 }
 

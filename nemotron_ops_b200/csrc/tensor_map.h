@@ -1,11 +1,11 @@
-// Tensor-map (TMA descriptor) helpers for streaming 16-row weight tiles with a 128-byte swizzle.
+// Tensor-map (TMA descriptor) helpers for streaming row tiles of weights with a 128-byte swizzle.
 //
 // A weight matrix of `rows` rows of `row_bytes` bytes (row_bytes % 128 == 0) is described as the
 // 3-D tensor (128-byte piece, row, piece index) with strides (1, row_bytes, 128).  A box of
-// (128, 16 rows, S pieces) lands in shared memory as [piece][row][128 B]; with the 128-byte
+// (128, BR rows, S pieces) lands in shared memory as [piece][row][128 B]; with the 128-byte
 // swizzle, the 16-byte chunks of smem line L are permuted by XOR with (L & 7), and line
-// L = piece * 16 + row, so eight consecutive rows of one piece sit in eight different bank
-// groups.  One request moves a whole (16 x S*128)-byte stage.
+// L = piece * BR + row (BR a multiple of 8), so eight consecutive rows of one piece sit in eight
+// different bank groups.  One request moves a whole (BR x S*128)-byte stage.
 #pragma once
 
 #include <cuda.h>
@@ -20,19 +20,22 @@ namespace bolt {
 // conflicts for 8- and 16-byte lane loads.
 //
 // Encodes (or returns the cached) map of `base` viewed as above with a box of
-// (piece_bytes, 16, pieces); piece_bytes is 128 (swizzled) or 16 (plain).  Returns false when
-// the view cannot be encoded (the caller then uses another path).
-bool row_tile_map(CUtensorMap* out, const void* base, int64_t rows, int64_t row_bytes, int pieces, int piece_bytes);
+// (piece_bytes, box_rows, pieces); piece_bytes is 128 (swizzled) or 16 (plain), box_rows a
+// multiple of 8 up to 256.  Returns false when the view cannot be encoded.
+bool row_tile_map(CUtensorMap* out, const void* base, int64_t rows, int64_t row_bytes, int pieces, int piece_bytes,
+                  int box_rows);
 
-// smem byte address of byte `b` of row `r` in a tile written by a row_tile_map box
-__device__ __forceinline__ uint32_t swz_off(int r, int b) {
-  return static_cast<uint32_t>((((b >> 7) * 16 + r) << 7) | ((((b >> 4) & 7) ^ (r & 7)) << 4) | (b & 15));
+// smem byte offset of byte `b` of row `r` in a tile of `br` rows written by a row_tile_map box
+__device__ __forceinline__ uint32_t swz_off(int r, int b, int br) {
+  return static_cast<uint32_t>((((b >> 7) * br + r) << 7) | ((((b >> 4) & 7) ^ (r & 7)) << 4) | (b & 15));
 }
-__device__ __forceinline__ uint32_t p16_off(int r, int b) {
-  return static_cast<uint32_t>((((b >> 4) * 16 + r) << 4) | (b & 15));
+__device__ __forceinline__ uint32_t p16_off(int r, int b, int br) {
+  return static_cast<uint32_t>((((b >> 4) * br + r) << 4) | (b & 15));
 }
 // sw: 1 = 128-byte swizzled pieces, 0 = 16-byte pieces
-__device__ __forceinline__ uint32_t tile_off(int sw, int r, int b) { return sw ? swz_off(r, b) : p16_off(r, b); }
+__device__ __forceinline__ uint32_t tile_off(int sw, int r, int b, int br) {
+  return sw ? swz_off(r, b, br) : p16_off(r, b, br);
+}
 
 // Pulls a tensor map into the descriptor cache ahead of its first use.
 __device__ __forceinline__ void prefetch_tensor_map(const CUtensorMap* map) {
