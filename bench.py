@@ -264,6 +264,61 @@ def max_over_ranks(v, world):
     return float(t.item())
 
 
+def sharded_moe_measure(world, rank, device, iq2=0, E=304, I=2304, R=8, topk=8, iters=30, warmup=5):
+    """Expert-sharded MoeVerify step: local shard kernel + fp32 NCCL all-reduce + bf16 cast.
+
+    Every rank routes the same seeded inputs and holds only its own experts' weights (rotated
+    copies larger than 3x L2).  Times are CUDA events on the compute stream, max over ranks."""
+    import torch.distributed as dist
+
+    from nemotron_ops_b200 import ops
+    from nemotron_ops_b200 import workloads as W
+    from nemotron_ops_b200.sharded import ShardedMoeVerify
+
+    r = W.moe_route(R=R, E=E, K=4096, seed=0, device=device)
+    idx, w, _ = ops.MoeRoute(r["x"], r["gate_w"], r["bias"], topk, 5.0)
+    z = W.moe_latent(R=R, device=device)
+    moe = ShardedMoeVerify(E, topk, iq2)
+    e0, e1 = moe.e_begin, moe.e_end
+    one = W.moe_experts(E=e1 - e0, I=I, iq2=iq2, seed=10 + rank, device=device)
+    per_copy = sum(t.numel() * t.element_size() for t in one.values())
+    copies = max(2, int((3 * L2_BYTES) // max(1, per_copy)) + 1)
+    sets = [one] + [W.moe_experts(E=e1 - e0, I=I, iq2=iq2, seed=20 + rank + 8 * c, device=device)
+                    for c in range(copies - 1)]
+    weights = [[d[k] for k in ("fc1_w", "fc1_s", "fc2_w", "fc2_s")] for d in sets]
+    ids = idx.reshape(-1).tolist()
+    local_uniq = len({e for e in ids if e0 <= e < e1})
+    per_expert = per_copy // (e1 - e0)
+
+    def run(i, reduce=True):
+        p = moe.partial(z, idx, w, weights[i % copies])
+        if reduce:
+            dist.all_reduce(p, op=dist.ReduceOp.SUM)
+        return ops.f32_to_bf16(p)
+
+    def timed(reduce):
+        for i in range(warmup):
+            run(i, reduce)
+        torch.cuda.synchronize()
+        barrier(world)
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record()
+        for i in range(iters):
+            run(i, reduce)
+        b.record()
+        torch.cuda.synchronize()
+        return max_over_ranks(a.elapsed_time(b) * 1e3 / iters, world)
+
+    us_total = timed(True)
+    us_compute = timed(False)
+    uniq_all = max_over_ranks(float(local_uniq), world)
+    return {"workload": f"sharded MoeVerify {'iq2=2' if iq2 else 'int4'} R={R} E={E} k={topk} I={I} over {world} GPUs",
+            "us_per_call": round(us_total, 2), "us_shard_compute": round(us_compute, 2),
+            "us_allreduce_and_cast": round(us_total - us_compute, 2),
+            "max_local_unique_experts": int(uniq_all), "bytes_max_rank": int(uniq_all * per_expert),
+            "experts_per_rank": e1 - e0}
+
+
 def capture(calls, reps):
     s = torch.cuda.Stream()
     s.wait_stream(torch.cuda.current_stream())
@@ -426,6 +481,15 @@ def main():
                 if "unique_experts" in r["wl"]:
                     extra[name]["unique_experts"] = r["wl"]["unique_experts"]
                 del r
+            except Exception as e:  # report, never hide
+                extra[name] = {"error": str(e)[:200]}
+            torch.cuda.empty_cache()
+
+    if world > 1 and not args.no_extra:  # the one path with a real exchange step
+        for q in (0, 2):
+            name = "moe_verify_sharded" + ("_iq2n" if q else "")
+            try:
+                extra[name] = sharded_moe_measure(world, rank, device, iq2=q)
             except Exception as e:  # report, never hide
                 extra[name] = {"error": str(e)[:200]}
             torch.cuda.empty_cache()

@@ -155,7 +155,9 @@ BOLT_API int bolt_moe_verify(const void* z, const int64_t* z_shape, int z_rank, 
  * experts, h / part rows of non-local pairs are left untouched, and
  *   out_partial f32 [R, 1024] = sum over local pairs of w * part  (k ascending)
  * is written for the caller to all-reduce (sum) across the shards; `out` (bf16, may be
- * NULL) receives bf16(out_partial).
+ * NULL) receives bf16(out_partial).  Only experts in [e_begin, e_end) are read, so a shard may
+ * hold just its own experts and pass fc1_w / fc1_s / fc2_w / fc2_s pointers shifted back by
+ * e_begin experts, with fc1_w_shape still giving the global expert count.
  */
 BOLT_API int bolt_moe_verify_shard(const void* z, const int64_t* z_shape, int z_rank, const void* idx, const void* w,
                           const void* fc1_w, const int64_t* fc1_w_shape, int fc1_w_rank, const void* fc1_s,

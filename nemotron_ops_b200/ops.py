@@ -136,16 +136,27 @@ def MoeVerify(z, idx, w, fc1_w, fc1_s, fc2_w, fc2_s, topk: int, iq2: int = 0):
     return out, h, part, meta
 
 
+def _expert_ptr(t, e_begin: int):
+    """Device address of expert 0 for a tensor holding experts [e_begin, ...) only (the kernels
+    read experts >= e_begin exclusively, so the shifted base is never dereferenced below them)."""
+    return ctypes.c_void_p(t.data_ptr() - int(e_begin) * t[0].numel() * t.element_size())
+
+
 def moe_verify_shard(z, idx, w, fc1_w, fc1_s, fc2_w, fc2_s, topk: int, iq2: int, e_begin: int, e_end: int,
-                     out_partial=None, outputs=None):
+                     num_experts: int = None, out_partial=None, outputs=None):
     """MoeVerify over experts [e_begin, e_end) only; returns (out_partial f32 [R, 1024], h, part, meta).
 
-    ``fc1_w`` etc. hold the full [E, ...] tensors (or views of a full-size allocation whose
-    non-local experts are never read).
+    The weight tensors hold either all ``num_experts`` experts, or only the local experts
+    [e_begin, e_end) (then ``num_experts`` gives the global count).  Rows of h / part of
+    non-local pairs are left untouched.
     """
     _need(z, idx, w, fc1_w, fc1_s, fc2_w, fc2_s)
     R = z.shape[0]
     P = R * topk
+    E = int(num_experts) if num_experts is not None else fc1_w.shape[0]
+    local = fc1_w.shape[0] != E
+    if local and fc1_w.shape[0] != e_end - e_begin:
+        raise RuntimeError("moe_verify_shard: local weights must hold exactly experts [e_begin, e_end)")
     if outputs is None:
         _, h, part = _moe_outputs(z, fc1_w, topk)
         meta = torch.empty(1 + P + 8 * P, dtype=torch.int32, device=z.device)
@@ -154,11 +165,12 @@ def moe_verify_shard(z, idx, w, fc1_w, fc1_s, fc2_w, fc2_s, topk: int, iq2: int,
     if out_partial is None:
         out_partial = torch.empty(R, 1024, dtype=torch.float32, device=z.device)
     zs, _k1 = shape_arg(z.shape)
-    w1s, _k2 = shape_arg(fc1_w.shape)
-    _check(lib().bolt_moe_verify_shard(_ptr(z), zs, z.dim(), _ptr(idx), _ptr(w), _ptr(fc1_w), w1s, fc1_w.dim(),
-                                       _ptr(fc1_s), _ptr(fc2_w), _ptr(fc2_s), int(topk), int(iq2), int(e_begin),
-                                       int(e_end), ctypes.c_void_p(0), _ptr(h), _ptr(part), _ptr(meta),
-                                       _ptr(out_partial), _stream(z)))
+    w1s, _k2 = shape_arg((E,) + tuple(fc1_w.shape[1:]))
+    wp = [_expert_ptr(t, e_begin) if local else _ptr(t) for t in (fc1_w, fc1_s, fc2_w, fc2_s)]
+    _check(lib().bolt_moe_verify_shard(_ptr(z), zs, z.dim(), _ptr(idx), _ptr(w), wp[0], w1s, fc1_w.dim(),
+                                       wp[1], wp[2], wp[3], int(topk), int(iq2), int(e_begin), int(e_end),
+                                       ctypes.c_void_p(0), _ptr(h), _ptr(part), _ptr(meta), _ptr(out_partial),
+                                       _stream(z)))
     return out_partial, h, part, meta
 
 

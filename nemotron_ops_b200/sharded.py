@@ -1,0 +1,75 @@
+"""Expert-parallel MoeVerify over torch.distributed: one process per GPU.
+
+The reference runs MoeVerify on one GPU (src/bolt_ops.cu:1178-1257).  Here rank g of G owns
+experts [g*E//G, (g+1)*E//G) and holds only their weights.  Every rank sees the same routing
+(MoeRoute is replicated), computes the fp32 partial output of the (token, expert) pairs whose
+expert is local (``bolt_moe_verify_shard``), and the partials are summed with one all-reduce
+(NCCL over NVLink on GPUs) before the bf16 cast.  Summing in fp32 keeps the result within fp32
+reassociation of the single-GPU op; a bf16 reduction would add a second rounding.
+
+The per-shard compute and the cast are the CUDA ops; both can be replaced by callables, which
+the CPU tests use to run the distributed logic on ``gloo`` ranks with the oracle as the shard
+computation.
+"""
+from __future__ import annotations
+
+from typing import Callable, Optional
+
+import torch
+import torch.distributed as dist
+
+__all__ = ["expert_range", "ShardedMoeVerify"]
+
+
+def expert_range(num_experts: int, rank: int, world: int):
+    """[e_begin, e_end) of the experts owned by ``rank``: contiguous, sizes differ by at most one."""
+    if world < 1 or not 0 <= rank < world:
+        raise ValueError("expert_range: need 0 <= rank < world")
+    return rank * num_experts // world, (rank + 1) * num_experts // world
+
+
+class ShardedMoeVerify:
+    """MoeVerify with experts sharded over the ranks of ``group``.
+
+    ``weights`` are this rank's slices ``(fc1_w, fc1_s, fc2_w, fc2_s)`` of experts
+    [e_begin, e_end) (use :meth:`local_slice` to cut them from full-size tensors).
+    """
+
+    def __init__(self, num_experts: int, topk: int, iq2: int = 0, group=None,
+                 shard_fn: Optional[Callable] = None, cast_fn: Optional[Callable] = None):
+        self.group = group
+        self.rank = dist.get_rank(group)
+        self.world = dist.get_world_size(group)
+        self.num_experts = int(num_experts)
+        self.topk = int(topk)
+        self.iq2 = int(iq2)
+        self.e_begin, self.e_end = expert_range(self.num_experts, self.rank, self.world)
+        self.shard_fn = shard_fn if shard_fn is not None else self._cuda_shard
+        self.cast_fn = cast_fn if cast_fn is not None else self._cuda_cast
+
+    def local_slice(self, t: torch.Tensor) -> torch.Tensor:
+        """This rank's experts of a full [E, ...] weight or scale tensor (contiguous copy)."""
+        return t[self.e_begin:self.e_end].contiguous()
+
+    def _cuda_shard(self, z, idx, w, weights, e_begin, e_end):
+        from . import ops
+        out_partial, _h, _part, _meta = ops.moe_verify_shard(z, idx, w, *weights, topk=self.topk, iq2=self.iq2,
+                                                             e_begin=e_begin, e_end=e_end,
+                                                             num_experts=self.num_experts)
+        return out_partial
+
+    @staticmethod
+    def _cuda_cast(t):
+        from . import ops
+        return ops.f32_to_bf16(t)
+
+    def partial(self, z, idx, w, weights) -> torch.Tensor:
+        """fp32 [R, 1024]: sum over this rank's pairs of w * part."""
+        return self.shard_fn(z, idx, w, weights, self.e_begin, self.e_end)
+
+    def __call__(self, z, idx, w, weights) -> torch.Tensor:
+        """bf16 [R, 1024] MoeVerify output, identical on every rank."""
+        p = self.partial(z, idx, w, weights)
+        if self.world > 1:
+            dist.all_reduce(p, op=dist.ReduceOp.SUM, group=self.group)
+        return self.cast_fn(p)

@@ -39,7 +39,7 @@ __all__ = [
     "FP4_VALUES", "IQ2_LUT_BF16", "iq2xxs_grid", "bf16_round", "unpack_nibbles",
     "q8_dequant", "q4_dequant", "nvfp4_dequant", "iq2_lut_dequant", "iq2n_dequant",
     "iq2n_dequant_gguf_style", "gemv_contract", "q8_gemv", "q4_gemv", "nvfp4_gemv",
-    "moe_route", "route_min_gap", "moe_group_meta", "moe_decode", "moe_verify", "moe_combine",
+    "moe_route", "route_min_gap", "moe_group_meta", "moe_decode", "moe_verify", "moe_combine", "moe_verify_partial",
     "moe_expert_weights",
 ]
 
@@ -372,3 +372,22 @@ def moe_combine(part: torch.Tensor, w: torch.Tensor, topk: int) -> torch.Tensor:
     pr = part.reshape(R, topk, 1024).to(torch.float64)
     wt = w.reshape(R, topk).to(device=part.device, dtype=torch.float64)
     return (wt.unsqueeze(-1) * pr).sum(1).to(torch.float32).to(torch.bfloat16)
+
+
+def moe_verify_partial(z, idx, w, fc1_w, fc1_s, fc2_w, fc2_s, topk: int, iq2: int, e_begin: int, e_end: int,
+                       num_experts: int = None):
+    """fp32 [R, 1024] = sum over the pairs whose expert is in [e_begin, e_end) of w * part
+    (fp64 sum, k ascending): one shard's share of the expert-parallel MoeVerify.  The weight
+    tensors hold all experts, or only experts [e_begin, e_end) when ``num_experts`` is given."""
+    E = fc1_w.shape[0] if num_experts is None else int(num_experts)
+    R = z.shape[0]
+    flat = idx.reshape(-1).to(torch.int64).cpu()
+    local = (flat >= e_begin) & (flat < e_end)
+    if fc1_w.shape[0] != E:  # local slices: renumber the local experts from 0
+        idx_l = torch.where(local, flat - e_begin, torch.full_like(flat, -1)).reshape(idx.shape).to(torch.int32)
+    else:
+        idx_l = torch.where(local, flat, torch.full_like(flat, -1)).reshape(idx.shape).to(torch.int32)
+    fmt = {0: "q4_mma", 1: "iq2_lut", 2: "iq2n"}[iq2]
+    _, _, part = _moe_pairs(z, idx_l.to(z.device), w, fc1_w, fc1_s, fc2_w, fc2_s, topk, fmt)
+    wt = w.reshape(R, topk).to(torch.float64) * local.reshape(R, topk).to(torch.float64).to(w.device)
+    return (wt.unsqueeze(-1) * part.reshape(R, topk, 1024).to(torch.float64)).sum(1).to(torch.float32)
