@@ -165,6 +165,19 @@ BOLT_API int bolt_moe_verify_shard(const void* z, const int64_t* z_shape, int z_
                           int64_t e_end, void* out, void* h, void* part, void* meta, void* out_partial, void* stream);
 
 /*
+ * Expert-sharded MoeDecode step (no counterpart in the reference).  As bolt_moe_verify_shard:
+ * only pairs whose expert is in [e_begin, e_end) are computed (h / part rows of the other pairs
+ * are left untouched), out_partial f32 [R, 1024] receives their weighted sum for the caller to
+ * all-reduce, and `out` (bf16, may be NULL) receives bf16(out_partial).  Exact fp32 weights.
+ * Requires I % 256 == 0; the weight pointers may be shifted back by e_begin experts as for
+ * bolt_moe_verify_shard.
+ */
+BOLT_API int bolt_moe_decode_shard(const void* z, const int64_t* z_shape, int z_rank, const void* idx, const void* w,
+                          const void* fc1_w, const int64_t* fc1_w_shape, int fc1_w_rank, const void* fc1_s,
+                          const void* fc2_w, const void* fc2_s, int64_t topk, int64_t e_begin, int64_t e_end,
+                          void* out, void* h, void* part, void* out_partial, void* stream);
+
+/*
  * out[i] = bf16(in[i]) for n f32 values (the cast after the shard all-reduce).
  */
 BOLT_API int bolt_f32_to_bf16(const void* in, void* out, int64_t n, void* stream);

@@ -268,9 +268,11 @@ int bolt_moe_route(const void* x, const int64_t* x_shape, int x_rank, const void
   });
 }
 
-int bolt_moe_decode(const void* z, const int64_t* z_shape, int z_rank, const void* idx, const void* w,
+namespace {
+int moe_decode_impl(const void* z, const int64_t* z_shape, int z_rank, const void* idx, const void* w,
                     const void* fc1_w, const int64_t* fc1_w_shape, int fc1_w_rank, const void* fc1_s, const void* fc2_w,
-                    const void* fc2_s, int64_t topk, void* out, void* h, void* part, void* stream) {
+                    const void* fc2_s, int64_t topk, int64_t e_begin, int64_t e_end, bool sharded, void* out, void* h,
+                    void* part, void* out_partial, void* stream) {
   return guarded([&] {
     const Shape zs{z_shape, z_rank}, w1s{fc1_w_shape, fc1_w_rank};
     const int64_t R = zs.dim(0);
@@ -279,15 +281,50 @@ int bolt_moe_decode(const void* z, const int64_t* z_shape, int z_rank, const voi
     const int64_t I = w1s.dim(1);
     require(I % 32 == 0 && I % 8 == 0 && I > 0, "MoeDecode: bad inter size");
     require(topk >= 1 && R * topk <= 128, "MoeDecode: rows*topk must be in [1,128]");
+    require(I <= 8192, "MoeDecode: inter size must be <= 8192");
     if (R == 0) return;
+    const int64_t E = w1s.dim(0);
+    if (!sharded) {
+      e_begin = 0;
+      e_end = E;
+    }
+    require(e_begin >= 0 && e_begin <= e_end && e_end <= E, "MoeDecode: expert range outside [0, E]");
+    require(!sharded || I % 256 == 0, "MoeDecode shard: inter size must be a multiple of 256");
     require_aligned({z, fc1_w, fc2_w}, "MoeDecode");
-    check_launch(launch_moe_decode(static_cast<const bf16*>(z), static_cast<const int*>(idx),
-                                   static_cast<const float*>(w), static_cast<const uint8_t*>(fc1_w),
-                                   static_cast<const bf16*>(fc1_s), static_cast<const uint8_t*>(fc2_w),
-                                   static_cast<const bf16*>(fc2_s), static_cast<int>(R), static_cast<int>(w1s.dim(0)),
-                                   static_cast<int>(I), static_cast<int>(topk), static_cast<bf16*>(out),
-                                   static_cast<bf16*>(h), static_cast<float*>(part), make_cfg(stream)));
+    const LaunchCfg cfg = make_cfg(stream);
+    if (I % 256 == 0 && aligned16(fc1_s) && aligned16(fc2_s)) {
+      check_launch(launch_moe_decode(static_cast<const bf16*>(z), static_cast<const int*>(idx),
+                                     static_cast<const float*>(w), static_cast<const uint8_t*>(fc1_w),
+                                     static_cast<const bf16*>(fc1_s), static_cast<const uint8_t*>(fc2_w),
+                                     static_cast<const bf16*>(fc2_s), static_cast<int>(R), static_cast<int>(E),
+                                     static_cast<int>(I), static_cast<int>(topk), static_cast<int>(e_begin),
+                                     static_cast<int>(e_end), static_cast<bf16*>(out), static_cast<bf16*>(h),
+                                     static_cast<float*>(part), static_cast<float*>(out_partial), cfg));
+    } else {
+      check_launch(launch_moe_decode_simt(static_cast<const bf16*>(z), static_cast<const int*>(idx),
+                                          static_cast<const float*>(w), static_cast<const uint8_t*>(fc1_w),
+                                          static_cast<const bf16*>(fc1_s), static_cast<const uint8_t*>(fc2_w),
+                                          static_cast<const bf16*>(fc2_s), static_cast<int>(R), static_cast<int>(E),
+                                          static_cast<int>(I), static_cast<int>(topk), static_cast<bf16*>(out),
+                                          static_cast<bf16*>(h), static_cast<float*>(part), cfg));
+    }
   });
+}
+}  // namespace
+
+int bolt_moe_decode(const void* z, const int64_t* z_shape, int z_rank, const void* idx, const void* w,
+                    const void* fc1_w, const int64_t* fc1_w_shape, int fc1_w_rank, const void* fc1_s, const void* fc2_w,
+                    const void* fc2_s, int64_t topk, void* out, void* h, void* part, void* stream) {
+  return moe_decode_impl(z, z_shape, z_rank, idx, w, fc1_w, fc1_w_shape, fc1_w_rank, fc1_s, fc2_w, fc2_s, topk, 0, 0,
+                         false, out, h, part, nullptr, stream);
+}
+
+int bolt_moe_decode_shard(const void* z, const int64_t* z_shape, int z_rank, const void* idx, const void* w,
+                          const void* fc1_w, const int64_t* fc1_w_shape, int fc1_w_rank, const void* fc1_s,
+                          const void* fc2_w, const void* fc2_s, int64_t topk, int64_t e_begin, int64_t e_end, void* out,
+                          void* h, void* part, void* out_partial, void* stream) {
+  return moe_decode_impl(z, z_shape, z_rank, idx, w, fc1_w, fc1_w_shape, fc1_w_rank, fc1_s, fc2_w, fc2_s, topk,
+                         e_begin, e_end, true, out, h, part, out_partial, stream);
 }
 
 int bolt_moe_verify(const void* z, const int64_t* z_shape, int z_rank, const void* idx, const void* w,

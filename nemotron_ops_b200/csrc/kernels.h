@@ -61,9 +61,15 @@ cudaError_t launch_dequant(int fmt, int exact, const uint8_t* w, const void* sc,
 cudaError_t launch_moe_route(const bf16* x, const bf16* gate_w, const float* bias, int R, int K, int E, int topk,
                              float scale, int* idx, float* w, float* scores, const LaunchCfg& cfg);
 
+// MoeDecode over the pairs whose expert is in [e_begin, e_end) (I % 256 == 0); out and/or
+// out_partial (fp32, the shard's share) may be null.
 cudaError_t launch_moe_decode(const bf16* z, const int* idx, const float* w, const uint8_t* fc1_w, const bf16* fc1_s,
-                              const uint8_t* fc2_w, const bf16* fc2_s, int R, int E, int I, int topk, bf16* out,
-                              bf16* h, float* part, const LaunchCfg& cfg);
+                              const uint8_t* fc2_w, const bf16* fc2_s, int R, int E, int I, int topk, int e_begin,
+                              int e_end, bf16* out, bf16* h, float* part, float* out_partial, const LaunchCfg& cfg);
+// MoeDecode for any I % 32 == 0 (SIMT), all experts.
+cudaError_t launch_moe_decode_simt(const bf16* z, const int* idx, const float* w, const uint8_t* fc1_w,
+                                   const bf16* fc1_s, const uint8_t* fc2_w, const bf16* fc2_s, int R, int E, int I,
+                                   int topk, bf16* out, bf16* h, float* part, const LaunchCfg& cfg);
 
 cudaError_t launch_moe_verify(int fmt, const bf16* z, const int* idx, const float* w, const uint8_t* fc1_w,
                               const bf16* fc1_s, const uint8_t* fc2_w, const bf16* fc2_s, int R, int E, int I,

@@ -1,20 +1,14 @@
-// MoeRoute / MoeDecode / MoeVerify kernels (reference src/bolt_ops.cu:359-619, :1078-1257).
+// MoeRoute kernels and the small kernels around the MoE expert GEMMs (reference
+// src/bolt_ops.cu:359-472, :552-587, :1084-1112); the expert GEMMs are in moe_tc.cu.
 //
 // MoeRoute: the fp32 router logits are one streaming dot per expert spread over all SMs (each
 // warp reads one gate row once and applies it to every activation row); the selection is one
 // warp per row: `topk` rounds of warp arg-max over score + bias with ties to the lower index.
 //
-// MoeDecode (exact fp32 weight contract, int4 zp 8): two persistent kernels chained with
-// programmatic dependent launch.  Both treat the P = R * topk (token, expert) pairs as
-// segments and give every CTA the same row range of every segment, so all CTAs stream the
-// same number of bytes.  fc1 writes h = bf16(relu(bf16(z . W1))^2); fc2 computes
-// part = float(bf16(h . W2)) for its output rows of every pair and finishes those rows of
-// `out` itself (the finalize needs no third kernel).  fc2 starts streaming its weights while
-// fc1 is still running.
-//
-// MoeVerify (tensor-core weight contract): a one-CTA grouping kernel writes the reference's
-// `meta` layout; the expert GEMMs run over a device-side work list of (unique expert, 16-row
-// tile) items sized from meta[0], so no CTA is launched for experts that were not selected.
+// MoeVerify grouping: one CTA writes the reference's `meta` layout (unique experts in
+// first-occurrence order and each expert's (token -> pair) map), restricted to a shard's expert
+// range.  Finalize: out = bf16(sum_k w * part), k ascending, over the pairs of the expert range,
+// optionally also as an fp32 partial for the sharded op.
 #include "mma_decode.cuh"
 
 namespace bolt {
@@ -118,12 +112,13 @@ __global__ void __launch_bounds__(32) router_topk_kernel(const float* __restrict
 }
 
 // =======================================================================================
-// MoeDecode: segmented exact-weight streaming GEMV (int4, zero point 8, bf16 block-32 scales)
+// MoeDecode, SIMT fallback for inter sizes that are not a multiple of 256: segmented
+// exact-weight streaming GEMV (int4, zero point 8, bf16 block-32 scales)
 // =======================================================================================
+constexpr int kMaxPairs = 128;
 constexpr int kSegWarps = 8;
 constexpr int kSegThreads = kSegWarps * 32;
 constexpr int kSegRows = 8;  // rows per stage
-constexpr int kMaxPairs = 128;
 
 struct SegParams {
   const bf16* x;         // fc1: z [R, K]; fc2: h [P, K]
@@ -374,7 +369,7 @@ __global__ void __launch_bounds__(kSegThreads, 1) moe_seg_kernel(const SegParams
 }
 
 // =======================================================================================
-// MoeVerify
+// MoeVerify grouping and the finalize
 // =======================================================================================
 // meta: [0] = U, [1 .. P] = unique expert ids in first-occurrence order (unused slots -1),
 // [1 + P + u * 8 + row] = pair index of `row` for unique expert u, or -1.
@@ -412,174 +407,6 @@ __global__ void __launch_bounds__(128) moe_group_kernel(const int* __restrict__ 
   if (p == 0) meta[0] = wtot[0] + wtot[1] + wtot[2] + wtot[3];
 }
 
-constexpr int kTile = 16;
-
-struct VerifyParams {
-  const bf16* xin;       // fc1: z [R, K]; fc2: h [P, K]
-  const int* meta;
-  const uint8_t* wq;     // [E, Nrows, row_bytes]
-  const uint8_t* sc;     // [E, Nrows, sc_row_bytes]
-  void* out;             // fc1: h bf16 [P, Nrows]; fc2: part f32 [P, Nrows]
-  int P, R, E, Nrows, K;
-  int nstage;
-  uint32_t stage_bytes;
-  uint32_t row_stride;
-  int early_weights;
-};
-
-// work item q: unique expert u = q / tpe, rows [16 * (q % tpe), +16) of that expert
-template <int FMT>
-__device__ __forceinline__ void verify_issue(const VerifyParams& p, uint8_t* smem, uint64_t* full_bar, int i, int q0,
-                                             int tpe, const int* uexp) {
-  const int slot_i = i % p.nstage;
-  const int q = q0 + i;
-  const int u = q / tpe;
-  const int n0 = (q % tpe) * kTile;
-  const int rows = min(kTile, p.Nrows - n0);
-  const int e = uexp[u];
-  const int64_t rb = fmt_row_bytes(FMT, p.K);
-  const int64_t srb = fmt_scale_row_bytes(FMT, p.K);
-  uint8_t* slot = smem + static_cast<size_t>(slot_i) * p.stage_bytes;
-  const uint32_t fb = smem_u32(&full_bar[slot_i]);
-  uint32_t tx = 0;
-  if (e >= 0 && e < p.E) {
-    const int64_t grow = static_cast<int64_t>(e) * p.Nrows + n0;
-    for (int r = 0; r < rows; ++r)
-      bulk_g2s(smem_u32(slot + r * p.row_stride), p.wq + (grow + r) * rb, static_cast<uint32_t>(rb), fb);
-    tx = static_cast<uint32_t>(rows * rb);
-    stage_span(slot + kTile * p.row_stride, p.sc + grow * srb, static_cast<uint32_t>(rows * srb),
-               p.sc + static_cast<int64_t>(p.E) * p.Nrows * srb, fb, tx);
-  }
-  mbar_arrive_expect_tx(fb, tx);
-}
-
-// PH 1: h[pair, j] = bf16(relu(bf16(z . W1[e, j]))^2); PH 2: part[pair, n] = float(bf16(h . W2[e, n]))
-template <int FMT, int PH, int KW, int CPW>
-__global__ void __launch_bounds__(KW * 32, 1) moe_verify_mma_kernel(const VerifyParams p) {
-  extern __shared__ __align__(128) uint8_t smem[];
-  __shared__ uint64_t full_bar[16];
-  __shared__ __align__(16) float red[2][KW][128];
-  __shared__ __align__(16) uint32_t grid_s[(FMT == kFmtIq2N) ? 1024 : 4];
-  __shared__ int uexp[kMaxPairs];
-  __shared__ int pmap[kMaxPairs][8];
-  __shared__ volatile int abort_flag;
-  __shared__ int s_u;
-
-  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  const int g = lane >> 2, t = lane & 3;
-  const int K = p.K;
-  const int tpe = (p.Nrows + kTile - 1) / kTile;
-  const int NS = p.nstage;
-  const int64_t srb = fmt_scale_row_bytes(FMT, K);
-
-  if (tid == 0) {
-    for (int s = 0; s < NS; ++s) mbar_init(smem_u32(&full_bar[s]), 1);
-    abort_flag = 0;
-    fence_barrier_init();
-  }
-  if constexpr (FMT == kFmtIq2N) {
-    for (int i = tid; i < 1024; i += blockDim.x) grid_s[i] = kIq2xxsGridBf16x2[i];
-  }
-  // PH 1 directly follows the grouping kernel, so it waits before reading the work list.  PH 2
-  // is released by PH 1 only after PH 1's own wait (meta complete), so it reads the work list
-  // (at L2) and starts streaming its weights while PH 1 still computes; it waits for PH 1's h
-  // before loading activations.
-  if (PH == 1) pdl_wait();
-  pdl_trigger();
-  if (tid == 0) s_u = ld_cg(p.meta);
-  for (int i = tid; i < p.P; i += blockDim.x) uexp[i] = ld_cg(p.meta + 1 + i);
-  for (int i = tid; i < p.P * 8; i += blockDim.x) pmap[i >> 3][i & 7] = ld_cg(p.meta + 1 + p.P + i);
-  __syncthreads();
-  const int U = s_u;
-  const int total = U * tpe;
-  const int q0 = static_cast<int>(static_cast<int64_t>(blockIdx.x) * total / gridDim.x);
-  const int q1 = static_cast<int>(static_cast<int64_t>(blockIdx.x + 1) * total / gridDim.x);
-  const int nq = q1 - q0;
-  if (tid == 0)
-    for (int i = 0; i < min(NS, nq); ++i) verify_issue<FMT>(p, smem, full_bar, i, q0, tpe, uexp);
-
-  if (PH == 2) pdl_wait();
-
-  const int nchunks = K >> 6;
-  const int cb = static_cast<int>(static_cast<int64_t>(warp) * nchunks / KW);
-  const int ce = static_cast<int>(static_cast<int64_t>(warp + 1) * nchunks / KW);
-  uint32_t bfr[CPW][8];
-  int xu = -1;  // unique expert whose activation rows are in bfr (PH 2)
-
-  for (int i = 0; i < nq; ++i) {
-    const int slot_i = i % NS;
-    const uint32_t ph = (i / NS) & 1;
-    const int q = q0 + i;
-    const int u = q / tpe;
-    const int n0 = (q % tpe) * kTile;
-    const int rows = min(kTile, p.Nrows - n0);
-    if ((PH == 1 && xu < 0) || (PH == 2 && u != xu)) {
-      xu = u;
-      int xrow;
-      bool valid;
-      if (PH == 1) {
-        xrow = g;
-        valid = g < p.R;
-      } else {
-        xrow = pmap[u][g];
-        valid = xrow >= 0;
-      }
-#pragma unroll
-      for (int j = 0; j < CPW; ++j) {
-        uint32_t x16[8] = {0, 0, 0, 0, 0, 0, 0, 0};
-        const int c = cb + j;
-        if (c < ce && valid) {
-          const uint4* xp = reinterpret_cast<const uint4*>(p.xin + static_cast<int64_t>(xrow) * K + 64 * c + 16 * t);
-          const uint4 a = xp[0], b = xp[1];
-          x16[0] = a.x; x16[1] = a.y; x16[2] = a.z; x16[3] = a.w;
-          x16[4] = b.x; x16[5] = b.y; x16[6] = b.z; x16[7] = b.w;
-        }
-        make_b_frags<FMT>(x16, bfr[j]);
-      }
-    }
-    if (!abort_flag && !mbar_wait(smem_u32(&full_bar[slot_i]), ph, kStatusFullWait)) abort_flag = 1;
-    const uint8_t* slot = smem + static_cast<size_t>(slot_i) * p.stage_bytes;
-    const int e = uexp[u];
-    const int64_t grow = static_cast<int64_t>(e >= 0 ? e : 0) * p.Nrows + n0;
-    const uint8_t* sc_base = slot + kTile * p.row_stride + (reinterpret_cast<uintptr_t>(p.sc + grow * srb) & 15);
-    float acc[4] = {0.f, 0.f, 0.f, 0.f};
-    if (e >= 0 && e < p.E) {
-#pragma unroll
-      for (int j = 0; j < CPW; ++j)
-        if (cb + j < ce)
-          mma_chunk<FMT>(slot + g * p.row_stride, slot + (g + 8) * p.row_stride, sc_base + g * srb,
-                         sc_base + (g + 8) * srb, cb + j, t, grid_s, bfr[j], acc);
-    }
-    const int buf = i & 1;
-    *reinterpret_cast<float2*>(&red[buf][warp][g * 8 + 2 * t]) = make_float2(acc[0], acc[1]);
-    *reinterpret_cast<float2*>(&red[buf][warp][(g + 8) * 8 + 2 * t]) = make_float2(acc[2], acc[3]);
-    asm volatile("bar.sync 1;" ::: "memory");
-    if (tid == 0 && i + NS < nq && !abort_flag) verify_issue<FMT>(p, smem, full_bar, i + NS, q0, tpe, uexp);
-    if (tid < 128) {
-      const int col = tid >> 4, rl = tid & 15;
-      const int pair = pmap[u][col];
-      if (rl < rows && pair >= 0 && e >= 0 && e < p.E) {
-        float v = 0.f;
-#pragma unroll
-        for (int w = 0; w < KW; ++w) v += red[buf][w][rl * 8 + col];
-        if constexpr (FmtTraits<FMT>::kF16) v *= 64.f;
-        v = __bfloat162float(__float2bfloat16(v));
-        const int64_t o = static_cast<int64_t>(pair) * p.Nrows + n0 + rl;
-        if constexpr (PH == 1) {
-          const float r = fmaxf(v, 0.f);
-          static_cast<bf16*>(p.out)[o] = __float2bfloat16(r * r);
-        } else {
-          static_cast<float*>(p.out)[o] = v;
-        }
-      }
-    }
-  }
-  if (tid == 0 && abort_flag)
-    for (int i = max(0, nq - NS); i < nq; ++i) mbar_wait(smem_u32(&full_bar[i % NS]), (i / NS) & 1, kStatusDrainWait);
-}
-
-// out[t, n] = sum_k w[t, k] * part[t * topk + k, n] over the pairs whose expert is in
-// [e_begin, e_end) (fp32, k ascending); bf16 into `out` and/or fp32 into `out_f32`.
 __global__ void __launch_bounds__(256) moe_finalize_kernel(const float* __restrict__ part, const float* __restrict__ w,
                                                            const int* __restrict__ idx, int R, int topk, int Nout,
                                                            int e_begin, int e_end, bf16* __restrict__ out,
@@ -642,41 +469,6 @@ cudaError_t dispatch_seg(SegParams& p, int grid, const LaunchCfg& cfg) {
   }
 }
 
-template <int FMT, int PH, int KW, int CPW>
-cudaError_t launch_verify_ph(const VerifyParams& p, int grid, const LaunchCfg& cfg) {
-  auto kern = moe_verify_mma_kernel<FMT, PH, KW, CPW>;
-  const size_t smem = static_cast<size_t>(p.nstage) * p.stage_bytes;
-  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
-  if (e != cudaSuccess) return e;
-  return launch_kernel(kern, dim3(grid), dim3(KW * 32), smem, cfg, p);
-}
-
-template <int FMT, int PH>
-cudaError_t dispatch_verify_ph(const VerifyParams& p, int grid, const LaunchCfg& cfg) {
-  const int nchunks = p.K >> 6;
-  if (nchunks <= 16) return launch_verify_ph<FMT, PH, 8, 2>(p, grid, cfg);
-  if (nchunks <= 32) return launch_verify_ph<FMT, PH, 8, 4>(p, grid, cfg);
-  if (nchunks <= 40) return launch_verify_ph<FMT, PH, 8, 5>(p, grid, cfg);
-  if (nchunks <= 64) return launch_verify_ph<FMT, PH, 8, 8>(p, grid, cfg);
-  return launch_verify_ph<FMT, PH, 16, 8>(p, grid, cfg);
-}
-
-VerifyParams make_verify_params(int fmt, const bf16* xin, const int* meta, const uint8_t* wq, const bf16* sc, void* out,
-                                int P, int R, int E, int Nrows, int K, const LaunchCfg& cfg, int grid) {
-  VerifyParams p{xin, meta, wq, reinterpret_cast<const uint8_t*>(sc), out, P, R, E, Nrows, K, 0, 0, 0,
-                 cfg.early_weights ? 1 : 0};
-  const int64_t rb = fmt_row_bytes(fmt, K);
-  const int bpc = fmt == kFmtIq2N ? 16 : 32;
-  const uint32_t pad = static_cast<uint32_t>((bpc - rb % 128 + 128) % 128);
-  p.row_stride = static_cast<uint32_t>(rb) + pad;
-  const uint32_t scb = static_cast<uint32_t>(kTile * fmt_scale_row_bytes(fmt, K) + 32);
-  p.stage_bytes = (kTile * p.row_stride + scb + 127) & ~127u;
-  const int fit = static_cast<int>((cfg.smem_budget ? cfg.smem_budget : 200 * 1024) / p.stage_bytes);
-  p.nstage = std::max(2, std::min(fit, 16));
-  (void)grid;
-  return p;
-}
-
 }  // namespace
 
 cudaError_t launch_moe_route(const bf16* x, const bf16* gate_w, const float* bias, int R, int K, int E, int topk,
@@ -690,7 +482,7 @@ cudaError_t launch_moe_route(const bf16* x, const bf16* gate_w, const float* bia
   return launch_kernel(router_topk_kernel, dim3(R), dim3(32), 0, c2, scores, bias, E, topk, scale, idx, w);
 }
 
-cudaError_t launch_moe_decode(const bf16* z, const int* idx, const float* w, const uint8_t* fc1_w, const bf16* fc1_s,
+cudaError_t launch_moe_decode_simt(const bf16* z, const int* idx, const float* w, const uint8_t* fc1_w, const bf16* fc1_s,
                               const uint8_t* fc2_w, const bf16* fc2_s, int R, int E, int I, int topk, bf16* out,
                               bf16* h, float* part, const LaunchCfg& cfg) {
   const int P = R * topk;
@@ -711,34 +503,14 @@ cudaError_t launch_moe_decode(const bf16* z, const int* idx, const float* w, con
   return dispatch_seg<2>(p2, grid2, c2);
 }
 
-cudaError_t launch_moe_verify(int fmt, const bf16* z, const int* idx, const float* w, const uint8_t* fc1_w,
-                              const bf16* fc1_s, const uint8_t* fc2_w, const bf16* fc2_s, int R, int E, int I,
-                              int topk, int e_begin, int e_end, bf16* out, bf16* h, float* part, int* meta,
-                              float* out_partial, const LaunchCfg& cfg) {
-  const int P = R * topk;
-  cudaError_t e = launch_kernel(moe_group_kernel, dim3(1), dim3(128), 0, cfg, idx, P, topk, e_begin, e_end, meta);
-  if (e != cudaSuccess) return e;
-  LaunchCfg c2 = cfg;
-  c2.pdl = true;
-  const int grid = cfg.sms;
-  VerifyParams p1 = make_verify_params(fmt, z, meta, fc1_w, fc1_s, h, P, R, E, I, 1024, c2, grid);
-  VerifyParams p2 = make_verify_params(fmt, h, meta, fc2_w, fc2_s, part, P, R, E, 1024, I, c2, grid);
-  switch (fmt) {
-    case kFmtQ4:
-      if ((e = dispatch_verify_ph<kFmtQ4, 1>(p1, grid, c2)) != cudaSuccess) return e;
-      if ((e = dispatch_verify_ph<kFmtQ4, 2>(p2, grid, c2)) != cudaSuccess) return e;
-      break;
-    case kFmtIq2Lut:
-      if ((e = dispatch_verify_ph<kFmtIq2Lut, 1>(p1, grid, c2)) != cudaSuccess) return e;
-      if ((e = dispatch_verify_ph<kFmtIq2Lut, 2>(p2, grid, c2)) != cudaSuccess) return e;
-      break;
-    default:
-      if ((e = dispatch_verify_ph<kFmtIq2N, 1>(p1, grid, c2)) != cudaSuccess) return e;
-      if ((e = dispatch_verify_ph<kFmtIq2N, 2>(p2, grid, c2)) != cudaSuccess) return e;
-      break;
-  }
+cudaError_t launch_moe_group(const int* idx, int P, int topk, int e_begin, int e_end, int* meta, const LaunchCfg& cfg) {
+  return launch_kernel(moe_group_kernel, dim3(1), dim3(128), 0, cfg, idx, P, topk, e_begin, e_end, meta);
+}
+
+cudaError_t launch_moe_finalize(const float* part, const float* w, const int* idx, int R, int topk, int e_begin,
+                                int e_end, bf16* out, float* out_partial, const LaunchCfg& cfg) {
   const int64_t n = static_cast<int64_t>(R) * 1024;
-  return launch_kernel(moe_finalize_kernel, dim3(static_cast<unsigned>((n + 255) / 256)), dim3(256), 0, c2, part, w,
+  return launch_kernel(moe_finalize_kernel, dim3(static_cast<unsigned>((n + 255) / 256)), dim3(256), 0, cfg, part, w,
                        idx, R, topk, 1024, e_begin, e_end, out, out_partial);
 }
 
