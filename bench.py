@@ -108,8 +108,8 @@ def _gemv_workload(kind, R, N, K, iq2=0):
 
         dt = {"nvfp4": "f16", "q8": "f32" if R == 1 else "bf16", "q4": "f32" if (R == 1 and iq2 == 0) else "bf16"}[kind]
         return dict(calls=calls, bytes=nbytes, kernels=1, h2d=R * K * 2, d2h=R * N * 2, e2e=e2e, cpu=cpu,
-                    cpu_sample=N, dtype=dt, kernel="gemv_mma_kernel" if kind == "nvfp4" or R > 1 or iq2 else
-                    "gemv_exact_kernel")
+                    cpu_sample=N, dtype=dt, kernel="gemv_exact_kernel" if (kind == "q8" and R == 1) else
+                    "gemv_tc_kernel")
     return build
 
 
@@ -163,8 +163,7 @@ def _moe_workload(op_name, R, iq2=0, E=304, I=2304, topk=8):
         kern = 3 if op_name == "MoeDecode" else 4
         return dict(calls=calls, bytes=nbytes, kernels=2 if op_name == "MoeDecode" else kern, h2d=R * 1024 * 2,
                     d2h=R * 1024 * 2, e2e=e2e, cpu=cpu, cpu_sample=R * topk, dtype="f32" if op_name == "MoeDecode"
-                    else "bf16", unique_experts=uniq, kernel="moe_seg_kernel" if op_name == "MoeDecode" else
-                    "moe_verify_mma_kernel")
+                    else "bf16", unique_experts=uniq, kernel="moe_tc_kernel")
     return build
 
 

@@ -174,6 +174,34 @@ def moe_verify_shard(z, idx, w, fc1_w, fc1_s, fc2_w, fc2_s, topk: int, iq2: int,
     return out_partial, h, part, meta
 
 
+def moe_decode_shard(z, idx, w, fc1_w, fc1_s, fc2_w, fc2_s, topk: int, e_begin: int, e_end: int,
+                     num_experts: int = None, out_partial=None, outputs=None):
+    """MoeDecode over experts [e_begin, e_end) only; returns (out_partial f32 [R, 1024], h, part).
+
+    Weight tensors as for :func:`moe_verify_shard` (all experts, or only the local ones with
+    ``num_experts`` giving the global count).  Requires I % 256 == 0.
+    """
+    _need(z, idx, w, fc1_w, fc1_s, fc2_w, fc2_s)
+    R = z.shape[0]
+    E = int(num_experts) if num_experts is not None else fc1_w.shape[0]
+    local = fc1_w.shape[0] != E
+    if local and fc1_w.shape[0] != e_end - e_begin:
+        raise RuntimeError("moe_decode_shard: local weights must hold exactly experts [e_begin, e_end)")
+    if outputs is None:
+        _, h, part = _moe_outputs(z, fc1_w, topk)
+    else:
+        h, part = outputs
+    if out_partial is None:
+        out_partial = torch.empty(R, 1024, dtype=torch.float32, device=z.device)
+    zs, _k1 = shape_arg(z.shape)
+    w1s, _k2 = shape_arg((E,) + tuple(fc1_w.shape[1:]))
+    wp = [_expert_ptr(t, e_begin) if local else _ptr(t) for t in (fc1_w, fc1_s, fc2_w, fc2_s)]
+    _check(lib().bolt_moe_decode_shard(_ptr(z), zs, z.dim(), _ptr(idx), _ptr(w), wp[0], w1s, fc1_w.dim(),
+                                       wp[1], wp[2], wp[3], int(topk), int(e_begin), int(e_end), ctypes.c_void_p(0),
+                                       _ptr(h), _ptr(part), _ptr(out_partial), _stream(z)))
+    return out_partial, h, part
+
+
 def f32_to_bf16(t, out=None):
     _need(t)
     if out is None:

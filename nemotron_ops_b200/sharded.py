@@ -1,11 +1,12 @@
-"""Expert-parallel MoeVerify over torch.distributed: one process per GPU.
+"""Expert-parallel MoeVerify and MoeDecode over torch.distributed: one process per GPU.
 
-The reference runs MoeVerify on one GPU (src/bolt_ops.cu:1178-1257).  Here rank g of G owns
-experts [g*E//G, (g+1)*E//G) and holds only their weights.  Every rank sees the same routing
-(MoeRoute is replicated), computes the fp32 partial output of the (token, expert) pairs whose
-expert is local (``bolt_moe_verify_shard``), and the partials are summed with one all-reduce
-(NCCL over NVLink on GPUs) before the bf16 cast.  Summing in fp32 keeps the result within fp32
-reassociation of the single-GPU op; a bf16 reduction would add a second rounding.
+The reference runs both ops on one GPU (MoeVerify src/bolt_ops.cu:1178-1257, MoeDecode
+:589-619).  Here rank g of G owns experts [g*E//G, (g+1)*E//G) and holds only their weights.
+Every rank sees the same routing (MoeRoute is replicated), computes the fp32 partial output of
+the (token, expert) pairs whose expert is local (``bolt_moe_verify_shard`` /
+``bolt_moe_decode_shard``), and the partials are summed with one all-reduce (NCCL over NVLink on
+GPUs) before the bf16 cast.  Summing in fp32 keeps the result within fp32 reassociation of the
+single-GPU op; a bf16 reduction would add a second rounding.
 
 The per-shard compute and the cast are the CUDA ops; both can be replaced by callables, which
 the CPU tests use to run the distributed logic on ``gloo`` ranks with the oracle as the shard
@@ -18,7 +19,7 @@ from typing import Callable, Optional
 import torch
 import torch.distributed as dist
 
-__all__ = ["expert_range", "ShardedMoeVerify"]
+__all__ = ["expert_range", "ShardedMoeVerify", "ShardedMoeDecode"]
 
 
 def expert_range(num_experts: int, rank: int, world: int):
@@ -29,7 +30,7 @@ def expert_range(num_experts: int, rank: int, world: int):
 
 
 class ShardedMoeVerify:
-    """MoeVerify with experts sharded over the ranks of ``group``.
+    """MoeVerify with experts sharded over the ranks of ``group`` (``iq2`` as the op's attribute).
 
     ``weights`` are this rank's slices ``(fc1_w, fc1_s, fc2_w, fc2_s)`` of experts
     [e_begin, e_end) (use :meth:`local_slice` to cut them from full-size tensors).
@@ -73,3 +74,17 @@ class ShardedMoeVerify:
         if self.world > 1:
             dist.all_reduce(p, op=dist.ReduceOp.SUM, group=self.group)
         return self.cast_fn(p)
+
+
+class ShardedMoeDecode(ShardedMoeVerify):
+    """MoeDecode (int4, exact fp32 weight contract) with experts sharded over ``group``."""
+
+    def __init__(self, num_experts: int, topk: int, group=None, shard_fn: Optional[Callable] = None,
+                 cast_fn: Optional[Callable] = None):
+        super().__init__(num_experts, topk, 0, group, shard_fn, cast_fn)
+
+    def _cuda_shard(self, z, idx, w, weights, e_begin, e_end):
+        from . import ops
+        out_partial, _h, _part = ops.moe_decode_shard(z, idx, w, *weights, topk=self.topk, e_begin=e_begin,
+                                                      e_end=e_end, num_experts=self.num_experts)
+        return out_partial

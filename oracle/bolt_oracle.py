@@ -40,6 +40,7 @@ __all__ = [
     "q8_dequant", "q4_dequant", "nvfp4_dequant", "iq2_lut_dequant", "iq2n_dequant",
     "iq2n_dequant_gguf_style", "gemv_contract", "q8_gemv", "q4_gemv", "nvfp4_gemv",
     "moe_route", "route_min_gap", "moe_group_meta", "moe_decode", "moe_verify", "moe_combine", "moe_verify_partial",
+    "moe_decode_partial",
     "moe_expert_weights",
 ]
 
@@ -379,6 +380,18 @@ def moe_verify_partial(z, idx, w, fc1_w, fc1_s, fc2_w, fc2_s, topk: int, iq2: in
     """fp32 [R, 1024] = sum over the pairs whose expert is in [e_begin, e_end) of w * part
     (fp64 sum, k ascending): one shard's share of the expert-parallel MoeVerify.  The weight
     tensors hold all experts, or only experts [e_begin, e_end) when ``num_experts`` is given."""
+    fmt = {0: "q4_mma", 1: "iq2_lut", 2: "iq2n"}[iq2]
+    return _moe_partial(z, idx, w, fc1_w, fc1_s, fc2_w, fc2_s, topk, fmt, e_begin, e_end, num_experts)
+
+
+def moe_decode_partial(z, idx, w, fc1_w, fc1_s, fc2_w, fc2_s, topk: int, e_begin: int, e_end: int,
+                       num_experts: int = None):
+    """One shard's share of the expert-parallel MoeDecode (exact fp32 weight contract); as
+    :func:`moe_verify_partial`."""
+    return _moe_partial(z, idx, w, fc1_w, fc1_s, fc2_w, fc2_s, topk, "q4_exact", e_begin, e_end, num_experts)
+
+
+def _moe_partial(z, idx, w, fc1_w, fc1_s, fc2_w, fc2_s, topk, fmt, e_begin, e_end, num_experts):
     E = fc1_w.shape[0] if num_experts is None else int(num_experts)
     R = z.shape[0]
     flat = idx.reshape(-1).to(torch.int64).cpu()
@@ -387,7 +400,6 @@ def moe_verify_partial(z, idx, w, fc1_w, fc1_s, fc2_w, fc2_s, topk: int, iq2: in
         idx_l = torch.where(local, flat - e_begin, torch.full_like(flat, -1)).reshape(idx.shape).to(torch.int32)
     else:
         idx_l = torch.where(local, flat, torch.full_like(flat, -1)).reshape(idx.shape).to(torch.int32)
-    fmt = {0: "q4_mma", 1: "iq2_lut", 2: "iq2n"}[iq2]
     _, _, part = _moe_pairs(z, idx_l.to(z.device), w, fc1_w, fc1_s, fc2_w, fc2_s, topk, fmt)
     wt = w.reshape(R, topk).to(torch.float64) * local.reshape(R, topk).to(torch.float64).to(w.device)
     return (wt.unsqueeze(-1) * part.reshape(R, topk, 1024).to(torch.float64)).sum(1).to(torch.float32)

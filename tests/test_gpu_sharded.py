@@ -1,4 +1,5 @@
-"""GPU parity of the expert-sharded MoeVerify step (bolt_moe_verify_shard through the C ABI).
+"""GPU parity of the expert-sharded MoeVerify and MoeDecode steps (bolt_moe_verify_shard,
+bolt_moe_decode_shard through the C ABI).
 
 The shards of a G-way split run one after another on one GPU, each with only its own experts'
 weights; their fp32 partials are summed and cast, as the all-reduce would do across GPUs.
@@ -57,4 +58,38 @@ def test_single_shard_equals_unsharded_op():
     args = [z, idx, w, ex["fc1_w"], ex["fc1_s"], ex["fc2_w"], ex["fc2_s"]]
     out = ops.MoeVerify(*args, topk=topk)[0]
     part, _, _, _ = ops.moe_verify_shard(*args, topk=topk, iq2=0, e_begin=0, e_end=E)
+    assert torch.equal(ops.f32_to_bf16(part), out)
+
+
+@pytest.mark.parametrize("G", [2, 8])
+@pytest.mark.parametrize("R,topk", [(1, 8), (3, 6)])
+def test_sharded_decode_partials_sum_to_the_op(G, R, topk):
+    E, I = 40, 512
+    ex = W.moe_experts(E=E, I=I, seed=7 + G)
+    z = W.moe_latent(R=R, seed=G + R)
+    idx, w = _routing(R, E, topk, seed=G + 1)
+    total = torch.zeros(R, 1024, dtype=torch.float64, device=DEV)
+    for g in range(G):
+        e0, e1 = expert_range(E, g, G)
+        local = [ex[k][e0:e1].contiguous() for k in ("fc1_w", "fc1_s", "fc2_w", "fc2_s")]
+        part, _, _ = ops.moe_decode_shard(z, idx, w, *local, topk=topk, e_begin=e0, e_end=e1, num_experts=E)
+        ref = O.moe_decode_partial(z, idx, w, ex["fc1_w"], ex["fc1_s"], ex["fc2_w"], ex["fc2_s"], topk, e0, e1)
+        err = (part.double() - ref.double()).abs()
+        assert bool((err <= 1e-3 + 1e-2 * ref.double().abs() + 1e-2 * ref.double().abs().max()).all())
+        total += part.double()
+    out = ops.f32_to_bf16(total.float())
+    ref_out = O.moe_decode(z, idx, w, ex["fc1_w"], ex["fc1_s"], ex["fc2_w"], ex["fc2_s"], topk=topk)[0]
+    rel = ((out.float() - ref_out.float()).norm() / ref_out.float().norm()).item()
+    assert rel < 1e-2
+    assert ops.device_status() == 0
+
+
+def test_single_shard_decode_equals_unsharded_op():
+    E, I, R, topk = 24, 256, 1, 8
+    ex = W.moe_experts(E=E, I=I, seed=4)
+    z = W.moe_latent(R=R, seed=4)
+    idx, w = _routing(R, E, topk, seed=4)
+    args = [z, idx, w, ex["fc1_w"], ex["fc1_s"], ex["fc2_w"], ex["fc2_s"]]
+    out = ops.MoeDecode(*args, topk=topk)[0]
+    part, _, _ = ops.moe_decode_shard(*args, topk=topk, e_begin=0, e_end=E)
     assert torch.equal(ops.f32_to_bf16(part), out)

@@ -1,4 +1,4 @@
-"""Expert-sharded MoeVerify: the distributed host logic on CPU ``gloo`` ranks.
+"""Expert-sharded MoeVerify and MoeDecode: the distributed host logic on CPU ``gloo`` ranks.
 
 The per-shard computation is the oracle's shard partial (the CUDA shard kernel is covered by
 ``tests/test_gpu_sharded.py``); what runs here is the product's partitioning, weight slicing,
@@ -13,7 +13,7 @@ import torch.distributed as dist
 import torch.multiprocessing as mp
 
 import oracle as O
-from nemotron_ops_b200.sharded import ShardedMoeVerify, expert_range
+from nemotron_ops_b200.sharded import ShardedMoeDecode, ShardedMoeVerify, expert_range
 from nemotron_ops_b200 import workloads as W
 
 
@@ -46,7 +46,7 @@ def _case(E, I, R, topk, iq2, seed):
     return z, idx, w, ex
 
 
-def _worker(rank, world, port, E, I, R, topk, iq2, seed, q):
+def _worker(rank, world, port, E, I, R, topk, iq2, seed, q, op="verify"):
     os.environ["MASTER_ADDR"] = "127.0.0.1"
     os.environ["MASTER_PORT"] = str(port)
     dist.init_process_group("gloo", rank=rank, world_size=world)
@@ -54,9 +54,15 @@ def _worker(rank, world, port, E, I, R, topk, iq2, seed, q):
         z, idx, w, ex = _case(E, I, R, topk, iq2, seed)
 
         def shard_fn(z_, idx_, w_, weights, e0, e1):
+            if op == "decode":
+                return O.moe_decode_partial(z_, idx_, w_, *weights, topk, e0, e1, num_experts=E)
             return O.moe_verify_partial(z_, idx_, w_, *weights, topk, iq2, e0, e1, num_experts=E)
 
-        moe = ShardedMoeVerify(E, topk, iq2, shard_fn=shard_fn, cast_fn=lambda t: t.to(torch.bfloat16))
+        cast = lambda t: t.to(torch.bfloat16)  # noqa: E731
+        if op == "decode":
+            moe = ShardedMoeDecode(E, topk, shard_fn=shard_fn, cast_fn=cast)
+        else:
+            moe = ShardedMoeVerify(E, topk, iq2, shard_fn=shard_fn, cast_fn=cast)
         weights = [moe.local_slice(ex[k]) for k in ("fc1_w", "fc1_s", "fc2_w", "fc2_s")]
         assert weights[0].shape[0] == moe.e_end - moe.e_begin
         out = moe(z, idx, w, weights)
@@ -83,6 +89,29 @@ def test_sharded_verify_matches_single_gpu_op(world, E, I, R, topk, iq2):
     assert [g[2:] for g in got] == [expert_range(E, r, world) for r in range(world)]
     for _, out, _, _ in got:
         # every rank holds the same all-reduced result; fp32 reassociation of the shard sums only
+        assert torch.equal(out, got[0][1])
+        err = (out.float() - ref.float()).abs()
+        assert bool((err <= 1e-3 + 1e-2 * ref.float().abs()).all())
+
+
+@pytest.mark.parametrize("world,E,I,R,topk", [(2, 8, 256, 1, 6), (3, 10, 256, 2, 4)])
+def test_sharded_decode_matches_single_gpu_op(world, E, I, R, topk):
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_worker, args=(r, world, port, E, I, R, topk, 0, 5, q, "decode"))
+             for r in range(world)]
+    for p in procs:
+        p.start()
+    got = [q.get(timeout=300) for _ in range(world)]
+    for p in procs:
+        p.join(timeout=120)
+        assert p.exitcode == 0
+    z, idx, w, ex = _case(E, I, R, topk, 0, 5)
+    ref = O.moe_decode(z, idx, w, ex["fc1_w"], ex["fc1_s"], ex["fc2_w"], ex["fc2_s"], topk=topk)[0]
+    got.sort(key=lambda g: g[0])
+    assert [g[2:] for g in got] == [expert_range(E, r, world) for r in range(world)]
+    for _, out, _, _ in got:
         assert torch.equal(out, got[0][1])
         err = (out.float() - ref.float()).abs()
         assert bool((err <= 1e-3 + 1e-2 * ref.float().abs()).all())
