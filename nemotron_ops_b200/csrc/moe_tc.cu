@@ -18,6 +18,7 @@
 // activation rows are bulk-copied into one of two shared buffers and converted in place into
 // B-fragment order (the other buffer still serves the previous group).  fc2 learns its experts
 // from meta before it waits for fc1, so its weights stream while fc1 finishes.
+#include <algorithm>
 #include <cstring>
 
 #include "mma_decode.cuh"
@@ -26,10 +27,8 @@ namespace bolt {
 
 namespace {
 
-constexpr int kCW = 8;                   // MMA warps
-constexpr int kThr = (kCW + 1) * 32;     // + producer warp
+// MMA warps per CTA (CW, 8 or 16) + 1 producer warp; one CTA per SM
 constexpr int kSlots = 8;
-constexpr int kRows = 32;                // rows per tile (two m16 tiles)
 
 struct MoeTcParams {
   const bf16* x;        // fc1: z [R, K]; fc2: h [P, K]
@@ -42,9 +41,10 @@ struct MoeTcParams {
   int verify;
   int fmt;
   int P, R, topk, K, rows_pg, E, e_begin, e_end;
+  int rows;             // rows per tile: 16 * MT
   int x_once;           // the activation rows are the same for every group: staged once
   int nxb;              // activation buffers (2: the next group's rows land during this group)
-  int kseg, nslot, pieces, wsw, smode, spieces;
+  int kseg, nslot, nsbuf, pieces, wsw, smode, spieces;
   uint32_t w_bytes, sc_bytes, xs_row, xs_buf, sc_off, xs_off, aux_off, red_off;
 };
 
@@ -73,8 +73,8 @@ __device__ __forceinline__ int column_xrow(const MoeTcParams& p, const int* lps,
   return FC == 1 ? pr / p.topk : pr;
 }
 
-__device__ __forceinline__ uint32_t sc_tile_off(int smode, int r, int b, int sc_rb) {
-  return smode ? p16_off(r, b, kRows) : static_cast<uint32_t>(r * sc_rb + b);
+__device__ __forceinline__ uint32_t sc_tile_off(int smode, int r, int b, int sc_rb, int rows) {
+  return smode ? p16_off(r, b, rows) : static_cast<uint32_t>(r * sc_rb + b);
 }
 
 // the CTA's tiles [t0, t1) of the flat (group, tile) list
@@ -106,17 +106,17 @@ __device__ __forceinline__ void issue_stage(const CUtensorMap* tmw, const CUtens
   const int s = st % p.nslot;
   const int ti = st / p.kseg, q = st % p.kseg;
   const int t = t0 + ti;
-  const int prow = expert * p.rows_pg + (t % tpg) * kRows;  // first physical row of the tile
+  const int prow = expert * p.rows_pg + (t % tpg) * p.rows;  // first physical row of the tile
   const uint32_t fb = smem_u32(&full_bar[s]);
   uint32_t tx = p.w_bytes;
   if (q == 0) {
-    uint8_t* sdst = smem + p.sc_off + static_cast<size_t>(ti & 1) * p.sc_bytes;
+    uint8_t* sdst = smem + p.sc_off + static_cast<size_t>(ti % p.nsbuf) * p.sc_bytes;
     if (p.smode) {
-      tx += static_cast<uint32_t>(p.spieces) * kRows * 16u;
+      tx += static_cast<uint32_t>(p.spieces) * p.rows * 16u;
       tma_load_3d(smem_u32(sdst), tms, 0, prow, 0, fb);
     } else {  // scale rows of a non-16-byte multiple: the tile's rows are one contiguous span
       const int64_t srb = fmt_scale_row_bytes(p.fmt, p.K);
-      stage_span(sdst, p.sc + static_cast<int64_t>(prow) * srb, static_cast<uint32_t>(kRows * srb),
+      stage_span(sdst, p.sc + static_cast<int64_t>(prow) * srb, static_cast<uint32_t>(p.rows * srb),
                  p.sc + static_cast<int64_t>(p.e_end) * p.rows_pg * srb, fb, tx);
     }
   }
@@ -124,16 +124,16 @@ __device__ __forceinline__ void issue_stage(const CUtensorMap* tmw, const CUtens
   mbar_arrive_expect_tx(fb, tx);
 }
 
-template <int FMT, bool BC, int CPW, bool FIX, int FC, int WM>
-__global__ void __launch_bounds__(kThr, 1)
+template <int FMT, bool BC, int CPW, bool FIX, int FC, int WM, int CW, int MT>
+__global__ void __launch_bounds__((CW + 1) * 32, 1)
     moe_tc_kernel(const __grid_constant__ CUtensorMap tmw, const __grid_constant__ CUtensorMap tms,
                   const MoeTcParams p) {
-  constexpr int MT = 2;
-  constexpr int ROWS = kRows;
+  constexpr int ROWS = 16 * MT;
   constexpr int GC = BC ? 4 : 1;  // block-column mode exists for Q4 (exact contract) only
   constexpr int BPC = 2;
   constexpr int NG = CPW / GC;
-  constexpr int KW = kCW / WM;    // warps along K
+  constexpr int KW = CW / WM;     // warps along K
+  constexpr int kThr = (CW + 1) * 32;
   static_assert(!BC || FMT == kFmtQ4, "MoE block-column mode is the int4 exact contract");
   extern __shared__ __align__(16) uint8_t smem_raw[];
   __shared__ uint64_t full_bar[kSlots], empty_bar[kSlots], x_bar[2];
@@ -155,7 +155,7 @@ __global__ void __launch_bounds__(kThr, 1)
   if (tid == 0) {
     for (int s = 0; s < NS; ++s) {
       mbar_init(smem_u32(&full_bar[s]), 1);
-      mbar_init(smem_u32(&empty_bar[s]), kCW);
+      mbar_init(smem_u32(&empty_bar[s]), CW);
     }
     mbar_init(smem_u32(&x_bar[0]), 1);
     mbar_init(smem_u32(&x_bar[1]), 1);
@@ -210,12 +210,12 @@ __global__ void __launch_bounds__(kThr, 1)
   const int g0 = t0 / tpg;
 
   // ------------------------------------------------------------------ producer warp
-  if (warp == kCW) {
+  if (warp == CW) {
     if (lane == 0 && ntl > 0) {
       prefetch_tensor_map(&tmw);
       if (p.smode) prefetch_tensor_map(&tms);
       // weights are constants and the expert list is ready: the first stages go out now
-      const int first = min(min(NS, nstages), 2 * KS);  // two scale buffers
+      const int first = min(min(NS, nstages), p.nsbuf * KS);  // a scale buffer per tile in flight
       int cur_e = -1, cur_g = -1;
       for (int st = 0; st < first; ++st) {
         const int g = (t0 + st / KS) / tpg;
@@ -234,8 +234,8 @@ __global__ void __launch_bounds__(kThr, 1)
         const int s = st % NS;
         const int ti = st / KS;
         bool okw = mbar_wait(smem_u32(&empty_bar[s]), ((st / NS) - 1) & 1, kStatusEmptyWait);
-        if (okw && st % KS == 0 && ti >= 2) {  // scale buffer of tile ti - 2 released
-          const int last = (ti - 1) * KS - 1;
+        if (okw && st % KS == 0 && ti >= p.nsbuf) {  // scale buffer of tile ti - nsbuf released
+          const int last = (ti - p.nsbuf + 1) * KS - 1;
           if (last > st - NS) okw = mbar_wait(smem_u32(&empty_bar[last % NS]), (last / NS) & 1, kStatusEmptyWait);
         }
         const int g = (t0 + ti) / tpg;
@@ -311,7 +311,7 @@ __global__ void __launch_bounds__(kThr, 1)
     int sb;
     if constexpr (BC) sb = 2 * (BPC * (cb + jg * GC) + 2 * t);
     else sb = chunk_scale_byte<FMT>(cb + jg, t);
-    soff[jg] = sc_tile_off(smode, pg, sb, sc_rb);
+    soff[jg] = sc_tile_off(smode, pg, sb, sc_rb, ROWS);
   }
 
   bool ok = true;
@@ -319,11 +319,13 @@ __global__ void __launch_bounds__(kThr, 1)
   uint32_t ph = 0;
   int xbuf = 0;
   const int ncol = p.verify ? 8 : 1;
+  // running tile bookkeeping (no divisions in the loop): group gg, tile tig within it, scale
+  // buffer sbuf, and the 16-byte misalignment of the group's plain-span scale rows
+  int gg = g0, tig = t0 - g0 * tpg, sbuf = 0;
+  uint32_t sc_mis = 0;
   for (int ti = 0; ti < ntl; ++ti) {
-    const int tt = t0 + ti;
-    const int gg = tt / tpg;
     const int kg = gg - g0;
-    if (ti == 0 || tt % tpg == 0) {  // a new group: its activations, in fragment order
+    if (ti == 0 || tig == 0) {  // a new group: its activations, in fragment order
       if (ti == 0 || !p.x_once) {
         xbuf = p.x_once ? 0 : kg % p.nxb;
         if (ok && !mbar_wait(smem_u32(&x_bar[xbuf]), (kg / p.nxb) & 1, kStatusFullWait)) {
@@ -336,16 +338,16 @@ __global__ void __launch_bounds__(kThr, 1)
           for (int j = 0; j < ncol; ++j) {
             if (column_xrow<FC>(p, lps, gg, j) < 0) continue;
             uint8_t* xr = xb + static_cast<size_t>(j) * p.xs_row;
-            for (int base = 0; base < np; base += 4 * kCW * 32) {
+            for (int base = 0; base < np; base += 4 * CW * 32) {
               uint4 v[4];
 #pragma unroll
               for (int k = 0; k < 4; ++k) {
-                const int pi = base + k * kCW * 32 + tid;
+                const int pi = base + k * CW * 32 + tid;
                 v[k] = pi < np ? lds128(xr + pi * 16) : make_uint4(0u, 0u, 0u, 0u);
               }
 #pragma unroll
               for (int k = 0; k < 4; ++k) {
-                const int pi = base + k * kCW * 32 + tid;
+                const int pi = base + k * CW * 32 + tid;
                 if (pi < np) *reinterpret_cast<uint4*>(xr + pi * 16) = x_piece_to_frag<FMT>(v[k]);
                 if constexpr (BC) {
                   const uint32_t w4[4] = {v[k].x, v[k].y, v[k].z, v[k].w};
@@ -362,12 +364,14 @@ __global__ void __launch_bounds__(kThr, 1)
         }
       }
       if (tid < 8) cols_s[kg & 1][tid] = tid < ncol ? column_pair(p, lps, gg, tid) : -1;
-      named_bar_sync(1, kCW * 32);
+      // plain-span scales land at the source's offset within 16 bytes; ROWS * sc_rb is a
+      // multiple of 16 (even scale rows), so the offset is the same for every tile of the group
+      if (!smode)
+        sc_mis = static_cast<uint32_t>(
+            reinterpret_cast<uintptr_t>(p.sc + static_cast<int64_t>(group_expert(p, lps, gg)) * p.rows_pg * sc_rb) & 15);
+      named_bar_sync(1, CW * 32);
     }
-    const uint8_t* sct = smem + p.sc_off + static_cast<size_t>(ti & 1) * p.sc_bytes;
-    if (!smode)  // plain span: the first byte landed at the source's offset within 16 bytes
-      sct += reinterpret_cast<uintptr_t>(p.sc + static_cast<int64_t>(group_expert(p, lps, gg) * p.rows_pg +
-                                                                     (tt % tpg) * ROWS) * sc_rb) & 15;
+    const uint8_t* sct = smem + p.sc_off + static_cast<size_t>(sbuf) * p.sc_bytes + sc_mis;
     const uint8_t* xq0 = xs + static_cast<size_t>(xbuf) * p.xs_buf;
     const float* xsm0 = xsum + xbuf * (K >> 5);
     float acc[MT][4];
@@ -458,9 +462,14 @@ __global__ void __launch_bounds__(kThr, 1)
             }
           }
         } else {
-          float acc2[MT][4];
+          // independent accumulator chains per m tile: chunk parity x k-step parity (MT <= 2),
+          // chunk parity (MT = 4)
+          constexpr int NX = MT <= 2 ? 3 : 1;
+          float accx[NX][MT][4];
 #pragma unroll
-          for (int m = 0; m < MT; ++m) acc2[m][0] = acc2[m][1] = acc2[m][2] = acc2[m][3] = 0.f;
+          for (int c = 0; c < NX; ++c)
+#pragma unroll
+            for (int m = 0; m < MT; ++m) accx[c][m][0] = accx[c][m][1] = accx[c][m][2] = accx[c][m][3] = 0.f;
 #pragma unroll
           for (int j = 0; j < CPW; ++j) {
             if (cb + j < ce) {
@@ -479,9 +488,13 @@ __global__ void __launch_bounds__(kThr, 1)
                   decode_row<FMT>(ra, t, grid_s, da);
                   decode_row<FMT>(rb, t, grid_s, db);
 #pragma unroll
-                  for (int s2 = 0; s2 < 4; ++s2)
-                    mma16816<false>((j & 1) ? acc2[m] : acc[m], da[2 * s2], db[2 * s2], da[2 * s2 + 1],
-                                    db[2 * s2 + 1], bf[2 * s2], bf[2 * s2 + 1]);
+                  for (int s2 = 0; s2 < 4; ++s2) {
+                    float(&dst)[4] = NX == 1 ? ((j & 1) ? accx[0][m] : acc[m])
+                                             : ((j & 1) ? ((s2 & 1) ? accx[NX - 1][m] : accx[NX > 1 ? 1 : 0][m])
+                                                        : ((s2 & 1) ? accx[0][m] : acc[m]));
+                    mma16816<false>(dst, da[2 * s2], db[2 * s2], da[2 * s2 + 1], db[2 * s2 + 1], bf[2 * s2],
+                                    bf[2 * s2 + 1]);
+                  }
                 }
               }
             }
@@ -489,7 +502,9 @@ __global__ void __launch_bounds__(kThr, 1)
 #pragma unroll
           for (int m = 0; m < MT; ++m)
 #pragma unroll
-            for (int e = 0; e < 4; ++e) acc[m][e] += acc2[m][e];
+            for (int c = 0; c < NX; ++c)
+#pragma unroll
+              for (int e = 0; e < 4; ++e) acc[m][e] += accx[c][m][e];
         }
       }
       __syncwarp();
@@ -497,7 +512,11 @@ __global__ void __launch_bounds__(kThr, 1)
       if (++s == NS) s = 0, ph ^= 1u;
     }
 
-    // ---- tile epilogue: sum the warps' partials, write h (fc1) or part (fc2) of the pairs
+    // ---- tile epilogue: sum the warps' partials, write h (fc1) or part (fc2) of the pairs.
+    // The partials go to one of two buffers (tile parity), so one barrier per tile suffices: a
+    // warp writes this buffer again two tiles later, after every warp has passed the barrier of
+    // the tile in between, i.e. after every warp has finished reading it.
+    float* redb = red + (ti & 1) * (CW * ROWS * (BC ? 1 : 8));
     if constexpr (BC) {
 #pragma unroll
       for (int m = 0; m < MT; ++m) {
@@ -507,26 +526,32 @@ __global__ void __launch_bounds__(kThr, 1)
         b += __shfl_xor_sync(0xffffffffu, b, 1);
         b += __shfl_xor_sync(0xffffffffu, b, 2);
         if (t == 0) {
-          red[warp * ROWS + 16 * m + pg] = a;
-          red[warp * ROWS + 16 * m + 8 + pg] = b;
+          redb[warp * ROWS + 16 * m + pg] = a;
+          redb[warp * ROWS + 16 * m + 8 + pg] = b;
         }
       }
     } else {
+      // [warp][row][8 columns], the column index XOR-swizzled by row bits 2..3 (pairs stay
+      // adjacent) so the column-major reads below spread over the banks
 #pragma unroll
       for (int m = 0; m < MT; ++m) {
-        *reinterpret_cast<float2*>(&red[(warp * ROWS + 16 * m + pg) * 8 + 2 * t]) = make_float2(acc[m][0], acc[m][1]);
-        *reinterpret_cast<float2*>(&red[(warp * ROWS + 16 * m + 8 + pg) * 8 + 2 * t]) = make_float2(acc[m][2], acc[m][3]);
+        const int ra = 16 * m + pg, rb = 16 * m + 8 + pg;
+        *reinterpret_cast<float2*>(&redb[(warp * ROWS + ra) * 8 + ((2 * t) ^ (((ra >> 2) & 3) << 1))]) =
+            make_float2(acc[m][0], acc[m][1]);
+        *reinterpret_cast<float2*>(&redb[(warp * ROWS + rb) * 8 + ((2 * t) ^ (((rb >> 2) & 3) << 1))]) =
+            make_float2(acc[m][2], acc[m][3]);
       }
     }
-    named_bar_sync(1, kCW * 32);
-    const int row0 = (tt % tpg) * ROWS;
-    for (int o = tid; o < ROWS * ncol; o += kCW * 32) {
+    named_bar_sync(1, CW * 32);
+    const int row0 = tig * ROWS;
+    for (int o = tid; o < ROWS * ncol; o += CW * 32) {
       const int col = o / ROWS, rl = o % ROWS;
       const int pr = cols_s[kg & 1][col];
       if (pr >= 0 && !abort_flag) {
         float v = 0.f;
+        const int cs = col ^ (((rl >> 2) & 3) << 1);
 #pragma unroll
-        for (int w = 0; w < kCW; ++w) v += BC ? red[w * ROWS + rl] : red[(w * ROWS + rl) * 8 + col];
+        for (int w = 0; w < CW; ++w) v += BC ? redb[w * ROWS + rl] : redb[(w * ROWS + rl) * 8 + cs];
         const float bv = __bfloat162float(__float2bfloat16(v));
         const int64_t oi = static_cast<int64_t>(pr) * p.rows_pg + row0 + rl;
         if constexpr (FC == 1) {
@@ -537,34 +562,52 @@ __global__ void __launch_bounds__(kThr, 1)
         }
       }
     }
-    named_bar_sync(1, kCW * 32);
+    if (++tig == tpg) tig = 0, ++gg;
+    if (++sbuf == p.nsbuf) sbuf = 0;
   }
 }
 
-template <int FMT, bool BC, int CPW, bool FIX, int FC, int WM>
+template <int FMT, bool BC, int CPW, bool FIX, int FC, int WM, int CW, int MT>
 cudaError_t launch_one(const CUtensorMap& tmw, const CUtensorMap& tms, const MoeTcParams& p, size_t smem,
                        const LaunchCfg& cfg) {
-  auto kern = moe_tc_kernel<FMT, BC, CPW, FIX, FC, WM>;
+  auto kern = moe_tc_kernel<FMT, BC, CPW, FIX, FC, WM, CW, MT>;
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
   if (e != cudaSuccess) return e;
-  return launch_kernel(kern, dim3(cfg.sms), dim3(kThr), smem, cfg, tmw, tms, p);
+  return launch_kernel(kern, dim3(cfg.sms), dim3((CW + 1) * 32), smem, cfg, tmw, tms, p);
 }
 
-template <int FMT, bool BC, int FC, int WM>
+template <int FMT, bool BC, int FC, int WM, int CW, int MT>
 cudaError_t dispatch_fix(int cpw, bool fix, const CUtensorMap& tmw, const CUtensorMap& tms, const MoeTcParams& p,
                          size_t smem, const LaunchCfg& cfg) {
   if constexpr (BC) {
     if (!fix) return cudaErrorInvalidValue;
-    if (cpw <= 4) return launch_one<FMT, BC, 4, true, FC, WM>(tmw, tms, p, smem, cfg);
-    return launch_one<FMT, BC, 8, true, FC, WM>(tmw, tms, p, smem, cfg);
+    if (cpw <= 4) return launch_one<FMT, BC, 4, true, FC, WM, CW, MT>(tmw, tms, p, smem, cfg);
+    return launch_one<FMT, BC, 8, true, FC, WM, CW, MT>(tmw, tms, p, smem, cfg);
   } else {
     static_assert(WM == 1, "grouped MMA path splits K only");
-    if (cpw <= 2) return fix ? launch_one<FMT, BC, 2, true, FC, 1>(tmw, tms, p, smem, cfg)
-                             : launch_one<FMT, BC, 2, false, FC, 1>(tmw, tms, p, smem, cfg);
-    if (cpw <= 4) return fix ? launch_one<FMT, BC, 4, true, FC, 1>(tmw, tms, p, smem, cfg)
-                             : launch_one<FMT, BC, 4, false, FC, 1>(tmw, tms, p, smem, cfg);
-    return fix ? launch_one<FMT, BC, 8, true, FC, 1>(tmw, tms, p, smem, cfg)
-               : launch_one<FMT, BC, 8, false, FC, 1>(tmw, tms, p, smem, cfg);
+    if (cpw <= 2) return fix ? launch_one<FMT, BC, 2, true, FC, 1, CW, MT>(tmw, tms, p, smem, cfg)
+                             : launch_one<FMT, BC, 2, false, FC, 1, CW, MT>(tmw, tms, p, smem, cfg);
+    if (cpw <= 4) return fix ? launch_one<FMT, BC, 4, true, FC, 1, CW, MT>(tmw, tms, p, smem, cfg)
+                             : launch_one<FMT, BC, 4, false, FC, 1, CW, MT>(tmw, tms, p, smem, cfg);
+    return fix ? launch_one<FMT, BC, 8, true, FC, 1, CW, MT>(tmw, tms, p, smem, cfg)
+               : launch_one<FMT, BC, 8, false, FC, 1, CW, MT>(tmw, tms, p, smem, cfg);
+  }
+}
+
+// dense (tensor-core contract) dispatch over the format and the tile height
+template <int FC>
+cudaError_t dispatch_dense(int fmt, int mt, int cpw, bool fix, const CUtensorMap& tmw, const CUtensorMap& tms,
+                           const MoeTcParams& p, size_t smem, const LaunchCfg& cfg) {
+  switch (fmt) {
+    case kFmtQ4:
+      return mt == 4 ? dispatch_fix<kFmtQ4, false, FC, 1, 8, 4>(cpw, fix, tmw, tms, p, smem, cfg)
+                     : dispatch_fix<kFmtQ4, false, FC, 1, 8, 2>(cpw, fix, tmw, tms, p, smem, cfg);
+    case kFmtIq2Lut:
+      return mt == 4 ? dispatch_fix<kFmtIq2Lut, false, FC, 1, 8, 4>(cpw, fix, tmw, tms, p, smem, cfg)
+                     : dispatch_fix<kFmtIq2Lut, false, FC, 1, 8, 2>(cpw, fix, tmw, tms, p, smem, cfg);
+    default:
+      return mt == 4 ? dispatch_fix<kFmtIq2N, false, FC, 1, 8, 4>(cpw, fix, tmw, tms, p, smem, cfg)
+                     : dispatch_fix<kFmtIq2N, false, FC, 1, 8, 2>(cpw, fix, tmw, tms, p, smem, cfg);
   }
 }
 
@@ -591,7 +634,14 @@ cudaError_t launch_grouped(int fmt, bool bc, int fc, bool verify, const bf16* x,
   p.e_begin = e_begin;
   p.e_end = e_end;
   p.x_once = (fc == 1 && (verify || R == 1)) ? 1 : 0;
-  if (rows_pg % kRows) return cudaErrorInvalidValue;
+  // tile height: 64 rows where every CTA still gets >= 8 tiles at the largest group count
+  // (halves the per-tile reduction and gives each warp four m tiles per B fragment), else 32
+  const int max_groups = verify ? std::min(P, e_end - e_begin) : P;
+  const int mt =
+      (!bc && rows_pg % 64 == 0 && static_cast<int64_t>(max_groups) * (rows_pg / 64) >= 8LL * cfg.sms) ? 4 : 2;
+  const int rows = 16 * mt;
+  p.rows = rows;
+  if (rows_pg % rows) return cudaErrorInvalidValue;
   const int64_t rb = fmt_row_bytes(fmt, K);
   const int64_t srb = fmt_scale_row_bytes(fmt, K);
   p.wsw = rb % 128 == 0 ? 1 : 0;
@@ -601,33 +651,36 @@ cudaError_t launch_grouped(int fmt, bool bc, int fc, bool verify, const bf16* x,
   const int gc = bc ? 4 : 1;
   p.smode = (srb % 16 == 0 && srb / 16 <= 256 && (reinterpret_cast<uintptr_t>(sc) & 15) == 0) ? 1 : 0;
   p.spieces = p.smode ? static_cast<int>(srb / 16) : 0;
-  p.sc_bytes = static_cast<uint32_t>((srb * kRows + (p.smode ? 0 : 32) + 127) & ~int64_t(127));
+  p.sc_bytes = static_cast<uint32_t>((srb * rows + (p.smode ? 0 : 32) + 127) & ~int64_t(127));
   const int ncol = verify ? 8 : 1;
   p.xs_row = static_cast<uint32_t>(nch) * 128u + (ncol > 1 ? 16u : 0u);
   p.xs_buf = (static_cast<uint32_t>(ncol) * p.xs_row + 127u) & ~127u;
   const size_t aux_bytes = (32 + (bc ? 2 * static_cast<size_t>(K / 32) * 4 : 0) + 127) & ~size_t(127);
-  const size_t red_bytes = static_cast<size_t>(kCW) * kRows * (bc ? 1 : 8) * sizeof(float);
+  const int cw = 8;  // MMA warps (16 measured no faster: the decode is issue-bound)
+  const size_t red_bytes = 2 * static_cast<size_t>(cw) * rows * (bc ? 1 : 8) * sizeof(float);
   const size_t budget = cfg.smem_budget ? cfg.smem_budget : 220 * 1024;
   // K segments: every MMA warp busy, stages within ~32 KB, at least two stages in the budget;
   // two activation buffers where they fit, else one (the next group's rows wait for this group)
+  // scale buffers: one per tile that the ring of ns stages can hold, plus the one being read
+  auto nsbuf_for = [](int ns, int kseg) { return std::min(kSlots, (ns + kseg - 1) / kseg + 1); };
   int ks = 0, wm = 1;
   size_t fixed = 0;
   for (int nxb = 2; nxb >= 1 && !ks; --nxb) {
     p.nxb = p.x_once ? 1 : nxb;
-    fixed = 1024 + 2 * static_cast<size_t>(p.sc_bytes) + static_cast<size_t>(p.nxb) * p.xs_buf + aux_bytes + red_bytes;
+    fixed = 1024 + static_cast<size_t>(p.nxb) * p.xs_buf + aux_bytes + red_bytes;
     for (int cand = 1; cand <= 64; ++cand) {
       if (pieces % cand || nch % cand || (nch / cand) % gc || srb % cand) continue;
       if (p.smode && (srb / cand) % 16) continue;
       if (fmt == kFmtIq2N && (nch / cand) % 4) continue;
       const int ng = nch / cand / gc;
-      const int kw = (bc && ng < kCW) ? kCW / 2 : kCW;
+      const int kw = (bc && ng < cw) ? cw / 2 : cw;
       if (ng < kw && ks) break;
       if (gc * ((ng + kw - 1) / kw) > 8) continue;
-      const size_t wb = (static_cast<size_t>(pieces / cand) * kRows * pb + 1023) & ~size_t(1023);
-      if (fixed + 2 * wb > budget) continue;
+      const size_t wb = (static_cast<size_t>(pieces / cand) * rows * pb + 1023) & ~size_t(1023);
+      if (fixed + 2 * wb + static_cast<size_t>(nsbuf_for(2, cand)) * p.sc_bytes > budget) continue;
       ks = cand;
-      wm = kCW / kw;
-      if (wb <= 32 * 1024) break;
+      wm = cw / kw;
+      if (wb <= static_cast<size_t>(rows) * 1024) break;
     }
     if (p.x_once) break;
   }
@@ -635,40 +688,35 @@ cudaError_t launch_grouped(int fmt, bool bc, int fc, bool verify, const bf16* x,
   p.kseg = ks;
   p.pieces = pieces / ks;
   CUtensorMap tmw, tms;
-  if (!row_tile_map(&tmw, w, static_cast<int64_t>(E) * rows_pg, rb, p.pieces, pb, kRows)) return cudaErrorInvalidValue;
-  if (p.smode && !row_tile_map(&tms, sc, static_cast<int64_t>(E) * rows_pg, srb, p.spieces, 16, kRows))
+  if (!row_tile_map(&tmw, w, static_cast<int64_t>(E) * rows_pg, rb, p.pieces, pb, rows)) return cudaErrorInvalidValue;
+  if (p.smode && !row_tile_map(&tms, sc, static_cast<int64_t>(E) * rows_pg, srb, p.spieces, 16, rows))
     return cudaErrorInvalidValue;
   if (!p.smode) std::memset(&tms, 0, sizeof(tms));
-  p.w_bytes = (static_cast<uint32_t>(p.pieces) * kRows * pb + 1023) & ~1023u;
+  p.w_bytes = (static_cast<uint32_t>(p.pieces) * rows * pb + 1023) & ~1023u;
   const int nchs = nch / ks;
-  const int kw = kCW / wm;
+  const int kw = cw / wm;
   const int cpw = gc * ((nchs / gc + kw - 1) / kw);
   const size_t xs_bytes = static_cast<size_t>(p.nxb) * p.xs_buf;
-  p.nslot = static_cast<int>(std::min<size_t>((budget - fixed) / p.w_bytes, kSlots));
+  for (p.nslot = kSlots; p.nslot > 2; --p.nslot)
+    if (fixed + static_cast<size_t>(p.nslot) * p.w_bytes + static_cast<size_t>(nsbuf_for(p.nslot, ks)) * p.sc_bytes <=
+        budget)
+      break;
+  p.nsbuf = nsbuf_for(p.nslot, ks);
   p.sc_off = static_cast<uint32_t>(static_cast<size_t>(p.nslot) * p.w_bytes);
-  p.xs_off = p.sc_off + 2 * p.sc_bytes;
+  p.xs_off = p.sc_off + static_cast<uint32_t>(p.nsbuf) * p.sc_bytes;
   p.aux_off = static_cast<uint32_t>(p.xs_off + xs_bytes);
   p.red_off = static_cast<uint32_t>(p.aux_off + aux_bytes);
   const size_t smem = 1024 + p.red_off + red_bytes;
   const bool fix = p.wsw == 1 && p.smode == 1;
-  if (bc) {
-    if (fmt != kFmtQ4) return cudaErrorInvalidValue;
-    if (fc == 1) return wm == 2 ? dispatch_fix<kFmtQ4, true, 1, 2>(cpw, fix, tmw, tms, p, smem, cfg)
-                                : dispatch_fix<kFmtQ4, true, 1, 1>(cpw, fix, tmw, tms, p, smem, cfg);
-    return wm == 2 ? dispatch_fix<kFmtQ4, true, 2, 2>(cpw, fix, tmw, tms, p, smem, cfg)
-                   : dispatch_fix<kFmtQ4, true, 2, 1>(cpw, fix, tmw, tms, p, smem, cfg);
+  if (bc) {  // block-column mode (32-row tiles)
+    if (fmt != kFmtQ4 || mt != 2) return cudaErrorInvalidValue;
+    if (fc == 1) return wm == 2 ? dispatch_fix<kFmtQ4, true, 1, 2, 8, 2>(cpw, fix, tmw, tms, p, smem, cfg)
+                                : dispatch_fix<kFmtQ4, true, 1, 1, 8, 2>(cpw, fix, tmw, tms, p, smem, cfg);
+    return wm == 2 ? dispatch_fix<kFmtQ4, true, 2, 2, 8, 2>(cpw, fix, tmw, tms, p, smem, cfg)
+                   : dispatch_fix<kFmtQ4, true, 2, 1, 8, 2>(cpw, fix, tmw, tms, p, smem, cfg);
   }
-  switch (fmt) {
-    case kFmtQ4:
-      return fc == 1 ? dispatch_fix<kFmtQ4, false, 1, 1>(cpw, fix, tmw, tms, p, smem, cfg)
-                     : dispatch_fix<kFmtQ4, false, 2, 1>(cpw, fix, tmw, tms, p, smem, cfg);
-    case kFmtIq2Lut:
-      return fc == 1 ? dispatch_fix<kFmtIq2Lut, false, 1, 1>(cpw, fix, tmw, tms, p, smem, cfg)
-                     : dispatch_fix<kFmtIq2Lut, false, 2, 1>(cpw, fix, tmw, tms, p, smem, cfg);
-    default:
-      return fc == 1 ? dispatch_fix<kFmtIq2N, false, 1, 1>(cpw, fix, tmw, tms, p, smem, cfg)
-                     : dispatch_fix<kFmtIq2N, false, 2, 1>(cpw, fix, tmw, tms, p, smem, cfg);
-  }
+  return fc == 1 ? dispatch_dense<1>(fmt, mt, cpw, fix, tmw, tms, p, smem, cfg)
+                 : dispatch_dense<2>(fmt, mt, cpw, fix, tmw, tms, p, smem, cfg);
 }
 
 }  // namespace
