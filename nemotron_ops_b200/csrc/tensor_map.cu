@@ -53,7 +53,8 @@ bool row_tile_map(CUtensorMap* out, const void* base, int64_t rows, int64_t row_
                   int box_rows) {
   static std::mutex mu;
   static std::unordered_map<Key, CUtensorMap, KeyHash> cache;
-  if ((piece_bytes != 128 && piece_bytes != 16) || row_bytes % piece_bytes != 0 || pieces < 1 || pieces > 256 ||
+  if ((piece_bytes != 128 && piece_bytes != 64 && piece_bytes != 16) || row_bytes % piece_bytes != 0 || pieces < 1 ||
+      pieces > 256 ||
       rows < 1 || box_rows < 8 || box_rows > 256 || box_rows % 8 || (reinterpret_cast<uintptr_t>(base) & 15))
     return false;
   int dev = 0;
@@ -74,7 +75,9 @@ bool row_tile_map(CUtensorMap* out, const void* base, int64_t rows, int64_t row_
   cuuint32_t box[3] = {static_cast<cuuint32_t>(pb), static_cast<cuuint32_t>(box_rows), static_cast<cuuint32_t>(pieces)};
   cuuint32_t estr[3] = {1, 1, 1};
   CUresult r = enc(&m, CU_TENSOR_MAP_DATA_TYPE_UINT8, 3, const_cast<void*>(base), dims, strides, box, estr,
-                   CU_TENSOR_MAP_INTERLEAVE_NONE, piece_bytes == 128 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_NONE,
+                   CU_TENSOR_MAP_INTERLEAVE_NONE,
+                   piece_bytes == 128 ? CU_TENSOR_MAP_SWIZZLE_128B
+                                      : (piece_bytes == 64 ? CU_TENSOR_MAP_SWIZZLE_64B : CU_TENSOR_MAP_SWIZZLE_NONE),
                    CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   if (r != CUDA_SUCCESS) return false;
   if (cache.size() > 4096) cache.clear();

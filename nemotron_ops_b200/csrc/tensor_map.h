@@ -19,9 +19,12 @@ namespace bolt {
 // [piece][row][16 B] interleaves the rows at 16-byte granularity, which is just as free of bank
 // conflicts for 8- and 16-byte lane loads.
 //
+// 64-byte pieces use the 64-byte swizzle: [piece][row][64 B] with the 16-byte chunks of each
+// row permuted by XOR with ((row >> 1) & 3), which spreads eight consecutive rows over the banks.
+//
 // Encodes (or returns the cached) map of `base` viewed as above with a box of
-// (piece_bytes, box_rows, pieces); piece_bytes is 128 (swizzled) or 16 (plain), box_rows a
-// multiple of 8 up to 256.  Returns false when the view cannot be encoded.
+// (piece_bytes, box_rows, pieces); piece_bytes is 128 or 64 (swizzled) or 16 (plain), box_rows
+// a multiple of 8 up to 256.  Returns false when the view cannot be encoded.
 bool row_tile_map(CUtensorMap* out, const void* base, int64_t rows, int64_t row_bytes, int pieces, int piece_bytes,
                   int box_rows);
 
