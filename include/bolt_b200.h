@@ -178,6 +178,23 @@ BOLT_API int bolt_moe_decode_shard(const void* z, const int64_t* z_shape, int z_
                           void* out, void* h, void* part, void* out_partial, void* stream);
 
 /*
+ * MoeVerify without caller-provided scratch (no counterpart in the reference).  Same inputs,
+ * output `out` and contract as bolt_moe_verify; its scratch outputs h, part and meta live in a
+ * static 1.5 MiB device buffer inside the library (one per device), so the call allocates
+ * nothing.  Limit: 8192 + R*topk*4096 + R*topk*I*2 bytes (each term rounded up to 256) must fit
+ * in 1,572,864 bytes, e.g. R = 8, topk = 8 with I <= 2304; larger calls fail with a message in
+ * bolt_last_error() -- use bolt_moe_verify with caller buffers for them.  The first call on a
+ * device looks the buffer's address up (cudaGetSymbolAddress); make it before capturing a stream
+ * into a CUDA graph.  Nothing has to start at zero: every scratch byte a call reads was written
+ * by the same call.  All calls on a device share the buffer, so calls that can overlap in time
+ * (different streams or threads) race: the caller must serialise them.
+ */
+BOLT_API int bolt_moe_verify_noalloc(const void* z, const int64_t* z_shape, int z_rank, const void* idx,
+                                     const void* w, const void* fc1_w, const int64_t* fc1_w_shape, int fc1_w_rank,
+                                     const void* fc1_s, const void* fc2_w, const void* fc2_s, int64_t topk,
+                                     int64_t iq2, void* out, void* stream);
+
+/*
  * out[i] = bf16(in[i]) for n f32 values (the cast after the shard all-reduce).
  */
 BOLT_API int bolt_f32_to_bf16(const void* in, void* out, int64_t n, void* stream);

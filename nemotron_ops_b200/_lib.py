@@ -23,6 +23,7 @@ SIGNATURES = {
     "bolt_moe_route": (_I, [_P, _S, _I, _P, _S, _I, _P, _L, ctypes.c_float, _P, _P, _P, _P]),
     "bolt_moe_decode": (_I, [_P, _S, _I, _P, _P, _P, _S, _I, _P, _P, _P, _L, _P, _P, _P, _P]),
     "bolt_moe_verify": (_I, [_P, _S, _I, _P, _P, _P, _S, _I, _P, _P, _P, _L, _L, _P, _P, _P, _P, _P]),
+    "bolt_moe_verify_noalloc": (_I, [_P, _S, _I, _P, _P, _P, _S, _I, _P, _P, _P, _L, _L, _P, _P]),
     "bolt_moe_verify_shard": (_I, [_P, _S, _I, _P, _P, _P, _S, _I, _P, _P, _P, _L, _L, _L, _L, _P, _P, _P, _P, _P,
                                    _P]),
     "bolt_moe_decode_shard": (_I, [_P, _S, _I, _P, _P, _P, _S, _I, _P, _P, _P, _L, _L, _L, _P, _P, _P, _P, _P]),

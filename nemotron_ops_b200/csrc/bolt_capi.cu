@@ -365,3 +365,70 @@ int bolt_dequant(int fmt, int exact, const void* w, const void* scales, int64_t 
 }
 
 }  // extern "C"
+
+// ---------------------------------------------------------------------------------------
+// MoeVerify without caller-provided scratch (no counterpart in the reference)
+// ---------------------------------------------------------------------------------------
+namespace {
+// Scratch of bolt_moe_verify_noalloc: meta, part and h of one call live here instead of in
+// caller buffers.  One buffer per device, shared by every call on that device.
+constexpr size_t kNoAllocScratchBytes = size_t(3) << 19;  // 1.5 MiB
+constexpr size_t kNoAllocMetaBytes = 8192;                 // meta of up to 128 pairs (4,612 bytes)
+static __device__ __align__(256) uint8_t g_noalloc_scratch[kNoAllocScratchBytes];
+
+constexpr int kMaxDevices = 64;
+std::mutex g_noalloc_mu;
+void* g_noalloc_ptr[kMaxDevices] = {};
+
+size_t round256(size_t n) { return (n + 255) & ~size_t(255); }
+
+// Device address of the scratch buffer of the current device (looked up once per device).
+void* noalloc_scratch() {
+  int dev = 0;
+  const cudaError_t e0 = cudaGetDevice(&dev);
+  if (e0 != cudaSuccess) throw std::runtime_error(std::string("MoeVerify (no-alloc): ") + cudaGetErrorString(e0));
+  if (dev < 0 || dev >= kMaxDevices) throw std::runtime_error("MoeVerify (no-alloc): device ordinal out of range");
+  std::lock_guard<std::mutex> lock(g_noalloc_mu);
+  if (!g_noalloc_ptr[dev]) {
+    void* p = nullptr;
+    const cudaError_t e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
+    if (e != cudaSuccess)
+      throw std::runtime_error(std::string("MoeVerify (no-alloc): cudaGetSymbolAddress failed: ") +
+                               cudaGetErrorString(e));
+    g_noalloc_ptr[dev] = p;
+  }
+  return g_noalloc_ptr[dev];
+}
+}  // namespace
+
+extern "C" {
+
+int bolt_moe_verify_noalloc(const void* z, const int64_t* z_shape, int z_rank, const void* idx, const void* w,
+                            const void* fc1_w, const int64_t* fc1_w_shape, int fc1_w_rank, const void* fc1_s,
+                            const void* fc2_w, const void* fc2_s, int64_t topk, int64_t iq2, void* out, void* stream) {
+  void* h = nullptr;
+  void* part = nullptr;
+  void* meta = nullptr;
+  const int rc = guarded([&] {
+    const Shape zs{z_shape, z_rank}, w1s{fc1_w_shape, fc1_w_rank};
+    const int64_t R = zs.dim(0), I = w1s.dim(1);
+    const int64_t P = R * topk;
+    require(R >= 1 && R <= 8 && topk >= 1 && P <= 128 && I > 0, "MoeVerify: rows must be in [1,8] and rows*topk <= 128");
+    const size_t part_bytes = round256(static_cast<size_t>(P) * 1024 * sizeof(float));
+    const size_t h_bytes = round256(static_cast<size_t>(P) * static_cast<size_t>(I) * 2);
+    const size_t need = kNoAllocMetaBytes + part_bytes + h_bytes;
+    if (need > kNoAllocScratchBytes)
+      throw std::invalid_argument("MoeVerify (no-alloc): rows*topk*(4096 + 2*I) needs " + std::to_string(need) +
+                                  " bytes of scratch, more than the " + std::to_string(kNoAllocScratchBytes) +
+                                  "-byte static buffer; use bolt_moe_verify with caller buffers");
+    uint8_t* base = static_cast<uint8_t*>(noalloc_scratch());
+    meta = base;
+    part = base + kNoAllocMetaBytes;
+    h = base + kNoAllocMetaBytes + part_bytes;
+  });
+  if (rc != BOLT_OK) return rc;
+  return bolt_moe_verify(z, z_shape, z_rank, idx, w, fc1_w, fc1_w_shape, fc1_w_rank, fc1_s, fc2_w, fc2_s, topk, iq2,
+                         out, h, part, meta, stream);
+}
+
+}  // extern "C"
