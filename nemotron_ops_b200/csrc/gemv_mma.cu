@@ -598,7 +598,11 @@ cudaError_t launch_gemv_mma(int fmt, const bf16* x, int R, const uint8_t* w, con
   const int pieces = static_cast<int>(rb / pb);
   const int nch = K >> 6;
   const int gc = bc ? (fmt == kFmtQ4 ? 4 : 2) : 1;
-  const int grid = static_cast<int>(std::min<int64_t>(cfg.sms, (N + 7) / 8));
+  // R = 1 without PDL: two CTAs per SM (measured 7-11% faster: more warps hide the decode and
+  // stream latency).  With PDL the second slot is left to the next call's CTAs, which stream
+  // their weights while this call computes; R > 1 keeps one CTA per SM (larger row tiles).
+  const int ctas = (R == 1 && !cfg.pdl) ? 2 * cfg.sms : cfg.sms;
+  const int grid = static_cast<int>(std::min<int64_t>(ctas, (N + 7) / 8));
   const int64_t rows_per_cta = (N + grid - 1) / grid;
   const int mt = rows_per_cta <= 16 ? 1 : 2;
   const int rows = 16 * mt;
