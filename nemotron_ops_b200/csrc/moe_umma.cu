@@ -481,6 +481,37 @@ __global__ void __launch_bounds__(kUThreads, 1)
         for (int kk = 0; kk < p.sp; ++kk) {
           const int ks = q * p.sp + kk;
           const int a = ka % kASlots;
+          // this thread's share of K step ks (weights, scales) goes to registers first; after the
+          // stage's last step the slot returns to the producer, so decoding does not hold it
+          constexpr int kU = FMT == kFmtQ4 ? 8 / kParts : 4 / kParts;  // 16-byte units
+          uint4 wv[kU];
+          uint32_t s4[kU];
+          float d = 0.f;
+          if (ok) {
+            if constexpr (FMT == kFmtQ4) {  // unit = 32 elements, one bf16 scale block each
+              const uint8_t* wp = wst + static_cast<size_t>(kk) * kTileRows * 128 + r * 128;
+              // (the host keeps int4 scale spans 16-byte aligned)
+              const uint8_t* spt = sct + r * sc_rb + ks * 16 + hh * (2 * kU);
+              if constexpr (kU == 4) {
+                const uint2 sv = *reinterpret_cast<const uint2*>(spt);
+                s4[0] = sv.x & 0xFFFFu, s4[1] = sv.x >> 16, s4[2] = sv.y & 0xFFFFu, s4[3] = sv.y >> 16;
+              } else {
+                const uint32_t sv = *reinterpret_cast<const uint32_t*>(spt);
+                s4[0] = sv & 0xFFFFu, s4[1] = sv >> 16;
+              }
+#pragma unroll
+              for (int i = 0; i < kU; ++i) wv[i] = lds128(wp + (((kU * hh + i) ^ (r & 7)) << 4));
+            } else {  // unit = two 32-element records
+              const uint8_t* wp = wst + static_cast<size_t>(kk) * kTileRows * 64 + r * 64;
+              d = __half2float(__ushort_as_half(*reinterpret_cast<const uint16_t*>(sct + r * sc_rb + ks * 2)));
+#pragma unroll
+              for (int i = 0; i < kU; ++i) wv[i] = lds128(wp + (((kU * hh + i) ^ ((r >> 1) & 3)) << 4));
+            }
+          }
+          if (kk == p.sp - 1) {  // the arrive releases (orders) the loads above
+            __syncwarp();
+            if (lane == 0) mbar_arrive(smem_u32(&empty_bar[s]));
+          }
           if (ok && abort_flag) ok = false;
           if (ok && ka >= kASlots && !mbar_wait(smem_u32(&ae_bar[a]), ((ka / kASlots) - 1) & 1, kStatusFullWait)) {
             ok = false;
@@ -492,21 +523,6 @@ __global__ void __launch_bounds__(kUThreads, 1)
             // [hh, hh + 1) * 128 / kParts of the A slot
             const uint32_t tcol = tb + lane_off + a_col(a) + (128u / kParts) * hh;
             if constexpr (FMT == kFmtQ4) {
-              constexpr int kU = 8 / kParts;  // 16-byte units (32 elements, one scale block each)
-              const uint8_t* wp = wst + static_cast<size_t>(kk) * kTileRows * 128 + r * 128;
-              // bf16 scales of the thread's blocks (the host keeps int4 scale spans 16-byte aligned)
-              uint32_t s4[kU];
-              const uint8_t* sp = sct + r * sc_rb + ks * 16 + hh * (2 * kU);
-              if constexpr (kU == 4) {
-                const uint2 sv = *reinterpret_cast<const uint2*>(sp);
-                s4[0] = sv.x & 0xFFFFu, s4[1] = sv.x >> 16, s4[2] = sv.y & 0xFFFFu, s4[3] = sv.y >> 16;
-              } else {
-                const uint32_t sv = *reinterpret_cast<const uint32_t*>(sp);
-                s4[0] = sv & 0xFFFFu, s4[1] = sv >> 16;
-              }
-              uint4 wv[kU];
-#pragma unroll
-              for (int i = 0; i < kU; ++i) wv[i] = lds128(wp + (((kU * hh + i) ^ (r & 7)) << 4));
 #pragma unroll
               for (int i = 0; i < kU; ++i) {
                 uint32_t o[16];
@@ -514,12 +530,6 @@ __global__ void __launch_bounds__(kUThreads, 1)
                 tc_st16(tcol + 16u * i, o);
               }
             } else {
-              constexpr int kU = 4 / kParts;  // 16-byte units (two 32-element records each)
-              const uint8_t* wp = wst + static_cast<size_t>(kk) * kTileRows * 64 + r * 64;
-              const float d = __half2float(__ushort_as_half(*reinterpret_cast<const uint16_t*>(sct + r * sc_rb + ks * 2)));
-              uint4 wv[kU];
-#pragma unroll
-              for (int i = 0; i < kU; ++i) wv[i] = lds128(wp + (((kU * hh + i) ^ ((r >> 1) & 3)) << 4));
 #pragma unroll
               for (int i = 0; i < kU; ++i) {
                 uint32_t o[16];
@@ -536,8 +546,6 @@ __global__ void __launch_bounds__(kUThreads, 1)
           if (lane == 0) mbar_arrive(smem_u32(&af_bar[a]));
           ++ka;
         }
-        __syncwarp();
-        if (lane == 0) mbar_arrive(smem_u32(&empty_bar[s]));
         if (++s == NS) s = 0, ph ^= 1u;
       }
       // the previous tile's accumulators are complete by now: drain them
@@ -600,10 +608,11 @@ cudaError_t launch_moe_layer_umma(int fmt, int fc, const bf16* x, const int* lis
   p.sc_rb = static_cast<int>(srb);
   // int4 scales are read as 8-byte words: the span of every tile must start 16-byte aligned
   if (fmt == kFmtQ4 && (srb % 16 || (reinterpret_cast<uintptr_t>(sc) & 15))) return cudaErrorNotSupported;
-  // pieces per stage: the largest divisor of the row's pieces with a stage of <= 32 KB
+  // pieces per stage: the largest divisor of the row's pieces with a stage of <= 48 KB (each
+  // tensor copy costs a fixed ~0.2-0.7 us to issue, more while the decode warps keep the SM busy)
   p.sp = 1;
   for (int c = 2; c <= pieces; ++c)
-    if (pieces % c == 0 && static_cast<size_t>(c) * kTileRows * p.pb <= 32 * 1024) p.sp = c;
+    if (pieces % c == 0 && static_cast<size_t>(c) * kTileRows * p.pb <= 48 * 1024) p.sp = c;
   p.kseg = pieces / p.sp;
   p.w_bytes = static_cast<uint32_t>(p.sp) * kTileRows * p.pb;
   p.w_stride = (p.w_bytes + 1023u) & ~1023u;
@@ -611,19 +620,23 @@ cudaError_t launch_moe_layer_umma(int fmt, int fc, const bf16* x, const int* lis
   p.xs_bytes = (static_cast<uint32_t>(8 * K * 2) + 1023u) & ~1023u;
   const size_t budget = cfg.smem_budget ? cfg.smem_budget : 220 * 1024;
   auto nsbuf_for = [](int ns, int kseg) { return std::min(4, (ns + kseg - 1) / kseg + 1); };
-  bool fit = false;
-  for (int nxb = p.x_once ? 1 : 2; nxb >= 1 && !fit; --nxb) {
-    p.nxb = nxb;
+  // one or two activation buffers: whichever leaves more weight bytes in flight (ties: two, so
+  // the next group's rows land while this group computes)
+  int best_nxb = 0, best_ns = 0;
+  for (int nxb = p.x_once ? 1 : 2; nxb >= 1; --nxb) {
     const size_t fixed = 1024 + static_cast<size_t>(nxb) * p.xs_bytes;
-    for (p.nslot = kUSlots; p.nslot >= 2; --p.nslot) {
-      p.nsbuf = nsbuf_for(p.nslot, p.kseg);
-      if (fixed + static_cast<size_t>(p.nslot) * p.w_stride + static_cast<size_t>(p.nsbuf) * p.sc_bytes <= budget) {
-        fit = true;
+    for (int ns = kUSlots; ns >= 2; --ns) {
+      if (fixed + static_cast<size_t>(ns) * p.w_stride + static_cast<size_t>(nsbuf_for(ns, p.kseg)) * p.sc_bytes <=
+          budget) {
+        if (ns > best_ns) best_nxb = nxb, best_ns = ns;
         break;
       }
     }
   }
-  if (!fit) return cudaErrorNotSupported;
+  if (!best_ns) return cudaErrorNotSupported;
+  p.nxb = best_nxb;
+  p.nslot = best_ns;
+  p.nsbuf = nsbuf_for(p.nslot, p.kseg);
   p.sc_off = static_cast<uint32_t>(p.nslot) * p.w_stride;
   p.xs_off = p.sc_off + static_cast<uint32_t>(p.nsbuf) * p.sc_bytes;
   p.xs_off = (p.xs_off + 1023u) & ~1023u;
