@@ -264,10 +264,11 @@ def max_over_ranks(v, world):
 
 
 def sharded_moe_measure(world, rank, device, iq2=0, E=304, I=2304, R=8, topk=8, iters=30, warmup=5):
-    """Expert-sharded MoeVerify step: local shard kernel + fp32 NCCL all-reduce + bf16 cast.
+    """Expert-sharded MoeVerify step: local shard kernels + fp32 NCCL all-reduce + bf16 cast.
 
     Every rank routes the same seeded inputs and holds only its own experts' weights (rotated
-    copies larger than 3x L2).  Times are CUDA events on the compute stream, max over ranks."""
+    copies larger than 3x L2).  The steps are replayed from a CUDA graph; times are CUDA events
+    on the compute stream, max over ranks."""
     import torch.distributed as dist
 
     from nemotron_ops_b200 import ops
@@ -289,24 +290,47 @@ def sharded_moe_measure(world, rank, device, iq2=0, E=304, I=2304, R=8, topk=8, 
     local_uniq = len({e for e in ids if e0 <= e < e1})
     per_expert = per_copy // (e1 - e0)
 
+    P = R * topk
+    out_p = torch.empty(R, 1024, dtype=torch.float32, device=device)
+    out = torch.empty(R, 1024, dtype=torch.bfloat16, device=device)
+    scratch = (torch.empty(P, I, dtype=torch.bfloat16, device=device),
+               torch.empty(P, 1024, dtype=torch.float32, device=device),
+               torch.empty(1 + P + 8 * P, dtype=torch.int32, device=device))
+
     def run(i, reduce=True):
-        p = moe.partial(z, idx, w, weights[i % copies])
+        ops.moe_verify_shard(z, idx, w, *weights[i % copies], topk=topk, iq2=iq2, e_begin=e0, e_end=e1,
+                             num_experts=E, out_partial=out_p, outputs=scratch)
         if reduce:
-            dist.all_reduce(p, op=dist.ReduceOp.SUM)
-        return ops.f32_to_bf16(p)
+            dist.all_reduce(out_p, op=dist.ReduceOp.SUM)
+        ops.f32_to_bf16(out_p, out=out)
 
     def timed(reduce):
+        # CUDA graph of `iters` steps (shard kernels, NCCL all-reduce, cast) over rotated weights,
+        # like the single-GPU legs; every rank captures and replays the same collectives
         for i in range(warmup):
             run(i, reduce)
         torch.cuda.synchronize()
         barrier(world)
+        side = torch.cuda.Stream()
+        side.wait_stream(torch.cuda.current_stream())
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.stream(side):
+            with torch.cuda.graph(g):
+                for i in range(iters):
+                    run(i, reduce)
+        torch.cuda.current_stream().wait_stream(side)
+        g.replay()
+        torch.cuda.synchronize()
+        barrier(world)
         a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         a.record()
-        for i in range(iters):
-            run(i, reduce)
+        g.replay()
         b.record()
         torch.cuda.synchronize()
-        return max_over_ranks(a.elapsed_time(b) * 1e3 / iters, world)
+        us = max_over_ranks(a.elapsed_time(b) * 1e3 / iters, world)
+        del g  # graphs holding NCCL calls go before the process group does
+        barrier(world)
+        return us
 
     us_total = timed(True)
     us_compute = timed(False)
