@@ -94,13 +94,26 @@ __device__ __forceinline__ void tc_commit(uint32_t bar) {
       " @e tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];\n}\n" ::"r"(bar)
       : "memory");
 }
-__device__ __forceinline__ void tc_mma(uint32_t d, uint32_t a, uint64_t bdesc, uint32_t accumulate) {
+// The 16 MMAs of one 256-element K step under a single election: MMA s reads A columns a + 8 s
+// (16 bf16 per lane) and B core matrices 2 s, 2 s + 1 (descriptor start + 16 in 16-byte units);
+// the first accumulates into D only when `accumulate` is set, the others always do.  The warp
+// issuing them shares its scheduler with decode warps, so each MMA costs three instructions.
+#define BOLT_MMA_NEXT                        \
+  " add.u32 a, a, 8;\n add.u64 b, b, 16;\n" \
+  " @e tcgen05.mma.cta_group::1.kind::f16 [%0], [a], b, %3, t;\n"
+__device__ __forceinline__ void tc_mma_kstep(uint32_t d, uint32_t a, uint64_t bdesc, uint32_t accumulate) {
   asm volatile(
-      "{\n .reg .pred p, e;\n setp.ne.b32 p, %4, 0;\n elect.sync _|e, 0xffffffff;\n"
-      " @e tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n}\n" ::"r"(d),
+      "{\n .reg .pred p, t, e;\n .reg .b32 a;\n .reg .b64 b;\n"
+      " setp.ne.b32 p, %4, 0;\n setp.ne.b32 t, %3, 0;\n mov.b32 a, %1;\n mov.b64 b, %2;\n"
+      " elect.sync _|e, 0xffffffff;\n"
+      " @e tcgen05.mma.cta_group::1.kind::f16 [%0], [a], b, %3, p;\n"
+      BOLT_MMA_NEXT BOLT_MMA_NEXT BOLT_MMA_NEXT BOLT_MMA_NEXT BOLT_MMA_NEXT BOLT_MMA_NEXT BOLT_MMA_NEXT
+      BOLT_MMA_NEXT BOLT_MMA_NEXT BOLT_MMA_NEXT BOLT_MMA_NEXT BOLT_MMA_NEXT BOLT_MMA_NEXT BOLT_MMA_NEXT
+      BOLT_MMA_NEXT "}\n" ::"r"(d),
       "r"(a), "l"(bdesc), "r"(kIdesc), "r"(accumulate)
       : "memory");
 }
+#undef BOLT_MMA_NEXT
 __device__ __forceinline__ void tc_st16(uint32_t taddr, const uint32_t (&v)[16]) {
   asm volatile(
       "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, "
@@ -362,9 +375,8 @@ __global__ void __launch_bounds__(kUThreads, 1)
           // K step ks starts at core matrix 32 * ks (128 bytes each, 8 in the descriptor's units)
           const uint64_t kdesc = xdesc + static_cast<uint64_t>(32 * ks) * 8u;
           const uint32_t dd = tb + d_col(b), aa = tb + a_col(a);
-#pragma unroll
-          for (int s = 0; s < kKStep / 16; ++s)
-            tc_mma(dd, aa + 8u * s, kdesc + static_cast<uint64_t>(2 * s) * 8u, (ks | s) != 0 ? 1u : 0u);
+          static_assert(kKStep == 16 * 16, "tc_mma_kstep issues 16 MMAs of K = 16");
+          tc_mma_kstep(dd, aa, kdesc, ks != 0 ? 1u : 0u);
           tc_commit(smem_u32(&ae_bar[a]));
           ++ka;
         }
