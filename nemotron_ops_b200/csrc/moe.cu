@@ -407,7 +407,10 @@ __global__ void __launch_bounds__(128) moe_group_kernel(const int* __restrict__ 
   if (p == 0) meta[0] = wtot[0] + wtot[1] + wtot[2] + wtot[3];
 }
 
-__global__ void __launch_bounds__(256) moe_finalize_kernel(const float* __restrict__ part, const float* __restrict__ w,
+// out[t] = sum over token t's local pairs of w * part (k ascending).  round_part: part holds fp32
+// sums; each pair's fc2 output is bf16(part), written back so part holds the per-pair outputs.
+__global__ void __launch_bounds__(256) moe_finalize_kernel(float* __restrict__ part, int round_part,
+                                                           const float* __restrict__ w,
                                                            const int* __restrict__ idx, int R, int topk, int Nout,
                                                            int e_begin, int e_end, bf16* __restrict__ out,
                                                            float* __restrict__ out_f32) {
@@ -420,7 +423,15 @@ __global__ void __launch_bounds__(256) moe_finalize_kernel(const float* __restri
   for (int k = 0; k < topk; ++k) {
     const int pp = t * topk + k;
     const int e = idx[pp];
-    if (e >= e_begin && e < e_end) a = fmaf(w[pp], part[static_cast<int64_t>(pp) * Nout + n], a);
+    if (e >= e_begin && e < e_end) {
+      const int64_t o = static_cast<int64_t>(pp) * Nout + n;
+      float v = part[o];
+      if (round_part) {
+        v = __bfloat162float(__float2bfloat16(v));
+        part[o] = v;
+      }
+      a = fmaf(w[pp], v, a);
+    }
   }
   if (out) out[i] = __float2bfloat16(a);
   if (out_f32) out_f32[i] = a;
@@ -507,11 +518,11 @@ cudaError_t launch_moe_group(const int* idx, int P, int topk, int e_begin, int e
   return launch_kernel(moe_group_kernel, dim3(1), dim3(128), 0, cfg, idx, P, topk, e_begin, e_end, meta);
 }
 
-cudaError_t launch_moe_finalize(const float* part, const float* w, const int* idx, int R, int topk, int e_begin,
-                                int e_end, bf16* out, float* out_partial, const LaunchCfg& cfg) {
+cudaError_t launch_moe_finalize(float* part, int round_part, const float* w, const int* idx, int R, int topk,
+                                int e_begin, int e_end, bf16* out, float* out_partial, const LaunchCfg& cfg) {
   const int64_t n = static_cast<int64_t>(R) * 1024;
-  return launch_kernel(moe_finalize_kernel, dim3(static_cast<unsigned>((n + 255) / 256)), dim3(256), 0, cfg, part, w,
-                       idx, R, topk, 1024, e_begin, e_end, out, out_partial);
+  return launch_kernel(moe_finalize_kernel, dim3(static_cast<unsigned>((n + 255) / 256)), dim3(256), 0, cfg, part,
+                       round_part, w, idx, R, topk, 1024, e_begin, e_end, out, out_partial);
 }
 
 }  // namespace bolt

@@ -723,12 +723,14 @@ cudaError_t launch_grouped(int fmt, bool bc, int fc, bool verify, const bf16* x,
 
 // group kernel (moe.cu): meta of the unique experts in [e_begin, e_end)
 cudaError_t launch_moe_group(const int* idx, int P, int topk, int e_begin, int e_end, int* meta, const LaunchCfg& cfg);
-cudaError_t launch_moe_finalize(const float* part, const float* w, const int* idx, int R, int topk, int e_begin,
-                                int e_end, bf16* out, float* out_partial, const LaunchCfg& cfg);
-// tcgen05 expert layer (moe_umma.cu); cudaErrorNotSupported when the shape or format does not fit
+// round_part: part holds fp32 fc2 sums, rounded to bf16 (and written back) here
+cudaError_t launch_moe_finalize(float* part, int round_part, const float* w, const int* idx, int R, int topk,
+                                int e_begin, int e_end, bf16* out, float* out_partial, const LaunchCfg& cfg);
+// tcgen05 expert layer (moe_umma.cu); cudaErrorNotSupported when the shape or format does not fit.
+// fc1 zeroes part_out when given one; fc2 with split relies on that to split tiles.
 cudaError_t launch_moe_layer_umma(int fmt, int fc, const bf16* x, const int* list, const uint8_t* w, const void* sc,
                                   bf16* h_out, float* part_out, int P, int R, int E, int e_end, int K, int rows_pg,
-                                  const LaunchCfg& cfg);
+                                  const LaunchCfg& cfg, int split);
 
 cudaError_t launch_moe_verify(int fmt, const bf16* z, const int* idx, const float* w, const uint8_t* fc1_w,
                               const bf16* fc1_s, const uint8_t* fc2_w, const bf16* fc2_s, int R, int E, int I,
@@ -740,17 +742,21 @@ cudaError_t launch_moe_verify(int fmt, const bf16* z, const int* idx, const floa
   LaunchCfg c2 = cfg;
   c2.pdl = true;  // same op: each kernel waits for its predecessor with griddepcontrol.wait
   // tcgen05 layers where they apply (int4 / native IQ2_XXS, 128-row tiles), else mma.sync
-  e = launch_moe_layer_umma(fmt, 1, z, meta, fc1_w, fc1_s, h, nullptr, P, R, E, e_end, 1024, I, c2);
+  // the tcgen05 fc1 also zeroes part (16-byte aligned), which lets the tcgen05 fc2 split tiles
+  const bool part16 = (reinterpret_cast<uintptr_t>(part) & 15) == 0;
+  e = launch_moe_layer_umma(fmt, 1, z, meta, fc1_w, fc1_s, h, part16 ? part : nullptr, P, R, E, e_end, 1024, I, c2,
+                            0);
+  const bool zeroed = e == cudaSuccess && part16;
   if (e == cudaErrorNotSupported)
     e = launch_grouped(fmt, false, 1, true, z, meta, idx, fc1_w, fc1_s, h, nullptr, P, R, topk, E, e_begin, e_end,
                        1024, I, c2);
   if (e != cudaSuccess) return e;
-  e = launch_moe_layer_umma(fmt, 2, h, meta, fc2_w, fc2_s, nullptr, part, P, R, E, e_end, I, 1024, c2);
+  e = launch_moe_layer_umma(fmt, 2, h, meta, fc2_w, fc2_s, nullptr, part, P, R, E, e_end, I, 1024, c2, zeroed ? 1 : 0);
   if (e == cudaErrorNotSupported)
     e = launch_grouped(fmt, false, 2, true, h, meta, idx, fc2_w, fc2_s, nullptr, part, P, R, topk, E, e_begin, e_end,
                        I, 1024, c2);
   if (e != cudaSuccess) return e;
-  return launch_moe_finalize(part, w, idx, R, topk, e_begin, e_end, out, out_partial, c2);
+  return launch_moe_finalize(part, 1, w, idx, R, topk, e_begin, e_end, out, out_partial, c2);
 }
 
 cudaError_t launch_moe_decode(const bf16* z, const int* idx, const float* w, const uint8_t* fc1_w, const bf16* fc1_s,
@@ -765,7 +771,7 @@ cudaError_t launch_moe_decode(const bf16* z, const int* idx, const float* w, con
   e = launch_grouped(kFmtQ4, true, 2, false, h, nullptr, idx, fc2_w, fc2_s, nullptr, part, P, R, topk, E, e_begin,
                      e_end, I, 1024, c2);
   if (e != cudaSuccess) return e;
-  return launch_moe_finalize(part, w, idx, R, topk, e_begin, e_end, out, out_partial, c2);
+  return launch_moe_finalize(part, 0, w, idx, R, topk, e_begin, e_end, out, out_partial, c2);
 }
 
 }  // namespace bolt

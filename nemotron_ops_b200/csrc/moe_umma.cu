@@ -13,8 +13,14 @@
 //     shared memory, K-major core matrices (8 rows x 16 bytes) without swizzle; the descriptor's
 //     8-row-group stride is 0, so columns 8..15 repeat columns 0..7 (N = 16 is the smallest
 //     N for M = 128);
-//   * D: fp32 in tensor memory, double-buffered so the epilogue of one tile (tcgen05.ld, bf16
-//     rounding, relu^2 for fc1) overlaps the MMAs of the next.
+//   * D: fp32 in tensor memory, double-buffered so the epilogue of one tile (tcgen05.ld; fc1:
+//     bf16 rounding, relu^2; fc2: fp32 partial sums) overlaps the MMAs of the next.
+// fc2 has 8 tiles per expert, few against 148 CTAs (40 experts: two or three tiles a CTA), so
+// its (tile, K segment) stages are divided evenly instead of its tiles: a tile may be split
+// between two CTAs at a stage boundary.  fc1 zeroes part_out; fc2 stores the fp32 sums of whole
+// tiles and adds (red.global.add) those of split ones -- with two addends on a zero the result
+// is a + b whichever lands first, so it stays deterministic.  The finalize kernel rounds the
+// per-pair outputs to bf16 (the contract's rounding of the fc2 output).
 // One elected thread issues the MMAs (16 per 256-element K step) as soon as the decode warps
 // have filled an A slot (three slots of 128 columns rotate); tcgen05.commit releases A slots,
 // completes D buffers and frees activation buffers through mbarriers.  The K reduction happens in
@@ -56,7 +62,9 @@ struct UmmaParams {
   const uint8_t* w;     // expert rows [E * rows_pg, row_bytes]
   const uint8_t* sc;    // [E * rows_pg, sc_row_bytes]
   bf16* h_out;          // fc1 output [P, rows_pg]
-  float* part_out;      // fc2 output [P, rows_pg]
+  float* part_out;      // fc2: fp32 output [P, rows_pg]; fc1: fc2's output [P, zero_cols] (or null)
+  int zero_cols;        // fc1: zeroes the part_out rows of the listed pairs, zero_cols floats each
+  int split;            // fc2: part_out starts zeroed, so a tile may be split between two CTAs
   int P, R, K, rows_pg, e_end;
   int x_once;           // fc1: the activation rows are the same for every group
   int nxb;              // activation buffers (2 where they fit)
@@ -198,12 +206,12 @@ __device__ __forceinline__ void issue_x(const UmmaParams& p, uint8_t* xs, uint64
 }
 
 // one weight stage (slot s, K segment q of the tile whose first physical row is prow; the tile's
-// scales go to scale buffer sb with its first segment)
+// scales go to scale buffer sb with the first segment this CTA reads of it, `scales`)
 __device__ __forceinline__ void issue_stage(const CUtensorMap* tmw, const UmmaParams& p, uint8_t* smem,
-                                            uint64_t* full_bar, int s, int q, int sb, int prow) {
+                                            uint64_t* full_bar, int s, int q, bool scales, int sb, int prow) {
   const uint32_t fb = smem_u32(&full_bar[s]);
   uint32_t tx = p.w_bytes;
-  if (q == 0) {  // the tile's scales (one contiguous span, one bulk copy) ride on its first stage
+  if (scales) {  // the tile's scales (one contiguous span, one bulk copy) ride on its first stage
     uint8_t* sdst = smem + p.sc_off + static_cast<size_t>(sb) * p.sc_bytes;
     const int64_t srb = p.sc_rb;
     stage_span(sdst, p.sc + static_cast<int64_t>(prow) * srb, static_cast<uint32_t>(kTileRows * srb),
@@ -229,7 +237,6 @@ __global__ void __launch_bounds__(kUThreads, 1)
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int KS = p.kseg, NS = p.nslot;
   const int tpg = p.rows_pg / kTileRows;
-  const int nks = p.K / kKStep;  // K steps per tile
   uint8_t* xs = smem + p.xs_off;
   if ((smem_u32(smem) & 1023u) != 0u || smem - smem_raw > 1023) {
     if (tid == 0) set_status(kStatusSmemAlign);
@@ -270,16 +277,47 @@ __global__ void __launch_bounds__(kUThreads, 1)
   if constexpr (FC == 1) {
     pdl_wait();  // meta is the previous kernel's output
     pdl_trigger();
+    // fc2's output rows of the listed pairs start at zero (this CTA's share of the 8 slots per
+    // group; other rows stay untouched; fc2 adds into them only after this grid completes)
+    if (p.part_out != nullptr) {
+      const int nslots = 8 * ldcg_i(p.list);
+      const int c4 = p.zero_cols >> 2;
+      for (int j = static_cast<int>(static_cast<int64_t>(blockIdx.x) * nslots / gridDim.x),
+               j1 = static_cast<int>(static_cast<int64_t>(blockIdx.x + 1) * nslots / gridDim.x);
+           j < j1; ++j) {
+        const int pp = ldcg_i(p.list + 1 + p.P + j);
+        if (pp < 0) continue;
+        float4* row = reinterpret_cast<float4*>(p.part_out + static_cast<int64_t>(pp) * p.zero_cols);
+        for (int i = tid; i < c4; i += kUThreads) row[i] = make_float4(0.f, 0.f, 0.f, 0.f);
+      }
+    }
   } else {
     pdl_trigger();
   }
   const int ngroups = ldcg_i(p.list);
   const int64_t T = static_cast<int64_t>(ngroups) * tpg;
-  const int t0 = static_cast<int>(static_cast<int64_t>(blockIdx.x) * T / gridDim.x);
-  const int t1 = static_cast<int>(static_cast<int64_t>(blockIdx.x + 1) * T / gridDim.x);
-  const int ntl = t1 - t0;
-  const int nstages = ntl * KS;
+  // This CTA's work: tiles [t0, t0 + ntl), K segments [seg_lo(ti), seg_hi(ti)) of tile ti.  fc2
+  // divides the flat list of (tile, K segment) stages evenly when there are at least as many tiles
+  // as CTAs, so every CTA takes at least one tile's worth and a tile is shared by at most two
+  // consecutive CTAs; fc1 (and fc2 with fewer tiles than CTAs) divides whole tiles.
+  int t0, ntl, q_first = 0, q_end = KS, nstages;
+  if (FC == 2 && p.split && T >= gridDim.x) {
+    const int64_t W = T * KS;
+    const int64_t f0 = static_cast<int64_t>(blockIdx.x) * W / gridDim.x;
+    const int64_t f1 = static_cast<int64_t>(blockIdx.x + 1) * W / gridDim.x;
+    t0 = static_cast<int>(f0 / KS);
+    q_first = static_cast<int>(f0 % KS);
+    ntl = static_cast<int>((f1 - 1) / KS) - t0 + 1;
+    q_end = static_cast<int>((f1 - 1) % KS) + 1;
+    nstages = static_cast<int>(f1 - f0);
+  } else {
+    t0 = static_cast<int>(static_cast<int64_t>(blockIdx.x) * T / gridDim.x);
+    ntl = static_cast<int>(static_cast<int64_t>(blockIdx.x + 1) * T / gridDim.x) - t0;
+    nstages = ntl * KS;
+  }
   const int g0 = ntl > 0 ? t0 / tpg : 0;
+  auto seg_lo = [&](int ti) { return ti == 0 ? q_first : 0; };
+  auto seg_hi = [&](int ti) { return ti == ntl - 1 ? q_end : KS; };
 
   if (warp == kProdW) {
     // ------------------------------------------------------------------ TMA producer
@@ -287,9 +325,10 @@ __global__ void __launch_bounds__(kUThreads, 1)
     // running counters instead of dividing (each of its instructions waits for an issue slot).
     if (lane == 0 && ntl > 0) {
       prefetch_tensor_map(&tmw);
-      const int first = min(min(NS, nstages), p.nsbuf * KS);  // a scale buffer per tile in flight
+      // a scale buffer per tile in flight
+      const int first = min(min(NS, nstages), p.nsbuf * KS - q_first);
       // stage cursor: slot s (use `round`), K segment q of tile ti (tile tig of group g), scale buffer sb
-      int s = 0, round = 0, q = 0, ti = 0, tig = t0 - g0 * tpg, g = g0, sb = 0;
+      int s = 0, round = 0, q = q_first, ti = 0, tig = t0 - g0 * tpg, g = g0, sb = 0;
       int cur_e = group_expert(p, g0);
       int prow = cur_e * p.rows_pg + tig * kTileRows;
       auto advance = [&]() {
@@ -308,7 +347,7 @@ __global__ void __launch_bounds__(kUThreads, 1)
       };
       int st = 0;
       for (; st < first; ++st) {
-        issue_stage(&tmw, p, smem, full_bar, s, q, sb, prow);
+        issue_stage(&tmw, p, smem, full_bar, s, q, q == seg_lo(ti), sb, prow);
         advance();
       }
       pdl_wait();  // activations (z, or h of fc1) are ready
@@ -334,16 +373,16 @@ __global__ void __launch_bounds__(kUThreads, 1)
         issue_x_upto(g);
         if (okw) okw = mbar_wait(smem_u32(&empty_bar[s]), (round - 1) & 1, kStatusEmptyWait);
         if (okw && q == 0 && ti >= p.nsbuf) {  // scale buffer of tile ti - nsbuf released
-          const int last = (ti - p.nsbuf + 1) * KS - 1;
+          const int last = (ti - p.nsbuf + 1) * KS - q_first - 1;  // its last stage
           if (last > st - NS) okw = mbar_wait(smem_u32(&empty_bar[last % NS]), (last / NS) & 1, kStatusEmptyWait);
         }
         if (!okw) abort_flag = 1;
         if (abort_flag) break;
-        issue_stage(&tmw, p, smem, full_bar, s, q, sb, prow);
+        issue_stage(&tmw, p, smem, full_bar, s, q, q == seg_lo(ti), sb, prow);
         ++issued;
         advance();
       }
-      issue_x_upto(g0 + (t1 - 1 - g0 * tpg) / tpg);  // groups whose stages all went out up front
+      issue_x_upto(g0 + (t0 + ntl - 1 - g0 * tpg) / tpg);  // groups whose stages all went out up front
       // no copy may still be landing when the CTA exits
       for (int b = 0; b <= min(xk, p.x_once ? 0 : p.nxb - 1); ++b) {
         const int k = xk - b;
@@ -366,7 +405,8 @@ __global__ void __launch_bounds__(kUThreads, 1)
         if (ok && ti >= 2) ok = mbar_wait(smem_u32(&de_bar[b]), ((ti - 2) >> 1) & 1, kStatusFullWait);
         ok = __all_sync(0xffffffffu, ok);
         const uint64_t xdesc = b_desc(smem_u32(xs + static_cast<size_t>(xb) * p.xs_bytes));
-        for (int ks = 0; ks < nks && ok; ++ks) {
+        const int ks_lo = seg_lo(ti) * p.sp, ks_hi = seg_hi(ti) * p.sp;
+        for (int ks = ks_lo; ks < ks_hi && ok; ++ks) {
           const int a = ka % kASlots;
           ok = !abort_flag && mbar_wait(smem_u32(&af_bar[a]), (ka / kASlots) & 1, kStatusFullWait);
           ok = __all_sync(0xffffffffu, ok);
@@ -376,7 +416,7 @@ __global__ void __launch_bounds__(kUThreads, 1)
           const uint64_t kdesc = xdesc + static_cast<uint64_t>(32 * ks) * 8u;
           const uint32_t dd = tb + d_col(b), aa = tb + a_col(a);
           static_assert(kKStep == 16 * 16, "tc_mma_kstep issues 16 MMAs of K = 16");
-          tc_mma_kstep(dd, aa, kdesc, ks != 0 ? 1u : 0u);
+          tc_mma_kstep(dd, aa, kdesc, ks != ks_lo ? 1u : 0u);
           tc_commit(smem_u32(&ae_bar[a]));
           ++ka;
         }
@@ -401,9 +441,11 @@ __global__ void __launch_bounds__(kUThreads, 1)
     uint32_t ph = 0;
     int ka = 0, gg = g0, tig = t0 - g0 * tpg, sbuf = 0;
     uint32_t sc_mis = 0;
-    int pend_ti = -1, pend_row0 = 0, pend_cols = 0;  // tile whose epilogue is pending
+    // tile whose epilogue is pending: its row, column slot and whether its sums cover all of K
+    int pend_ti = -1, pend_row0 = 0, pend_cols = 0;
+    bool pend_whole = true;
 
-    auto epilogue = [&](int tj, int row0, int cslot) {
+    auto epilogue = [&](int tj, int row0, int cslot, bool whole) {
       const int b = tj & 1;
       constexpr int kCols = 8 / kParts;  // token columns drained by this warp
       uint32_t v[kCols];
@@ -428,13 +470,14 @@ __global__ void __launch_bounds__(kUThreads, 1)
         for (int c = 0; c < kCols; ++c) {
           const int pr = cols_s[cslot][kCols * hh + c];
           if (pr < 0) continue;
-          const float bv = __bfloat162float(__float2bfloat16(__uint_as_float(v[c])));
           const int64_t oi = static_cast<int64_t>(pr) * p.rows_pg + row0 + r;
           if constexpr (FC == 1) {
-            const float rr = fmaxf(bv, 0.f);
+            const float rr = fmaxf(__bfloat162float(__float2bfloat16(__uint_as_float(v[c]))), 0.f);
             p.h_out[oi] = __float2bfloat16(rr * rr);  // rr * rr is exact in fp32
           } else {
-            p.part_out[oi] = bv;
+            // fp32 sums (the finalize kernel rounds them); a split tile's two K ranges add up
+            if (whole) p.part_out[oi] = __uint_as_float(v[c]);
+            else atomicAdd(p.part_out + oi, __uint_as_float(v[c]));
           }
         }
       }
@@ -482,7 +525,7 @@ __global__ void __launch_bounds__(kUThreads, 1)
         named_bar_sync(1, kDecW * 32);
       }
       const uint8_t* sct = smem + p.sc_off + static_cast<size_t>(sbuf) * p.sc_bytes + sc_mis;
-      for (int q = 0; q < KS; ++q) {
+      for (int q = seg_lo(ti); q < seg_hi(ti); ++q) {
         if (ok && abort_flag) ok = false;
         if (ok && !mbar_wait(smem_u32(&full_bar[s]), ph, kStatusFullWait)) {
           ok = false;
@@ -561,14 +604,15 @@ __global__ void __launch_bounds__(kUThreads, 1)
         if (++s == NS) s = 0, ph ^= 1u;
       }
       // the previous tile's accumulators are complete by now: drain them
-      if (pend_ti >= 0) epilogue(pend_ti, pend_row0, pend_cols);
+      if (pend_ti >= 0) epilogue(pend_ti, pend_row0, pend_cols, pend_whole);
       pend_ti = ti;
       pend_row0 = tig * kTileRows;
       pend_cols = kg % 3;
+      pend_whole = seg_lo(ti) == 0 && seg_hi(ti) == KS;
       if (++tig == tpg) tig = 0, ++gg;
       if (++sbuf == p.nsbuf) sbuf = 0;
     }
-    if (pend_ti >= 0) epilogue(pend_ti, pend_row0, pend_cols);
+    if (pend_ti >= 0) epilogue(pend_ti, pend_row0, pend_cols, pend_whole);
   }
   // release the tensor memory once every MMA and every tensor-memory access has finished
   tc_fence_before();
@@ -592,11 +636,13 @@ cudaError_t launch_umma(const CUtensorMap& tmw, const UmmaParams& p, size_t smem
 }  // namespace
 
 // One MoeVerify expert layer (fc1: K = 1024, rows_pg = I; fc2: K = I, rows_pg = 1024) on the
-// tcgen05 path.  cudaErrorNotSupported when the shapes or the format do not fit it (the caller
-// then uses the mma.sync kernel of moe_tc.cu).
+// tcgen05 path.  fc1 with part_out set zeroes the listed pairs' rows of part_out [P, 1024] (fc2's
+// output); fc2 with split (those rows zeroed) divides its stages evenly, splitting tiles between
+// CTAs.  cudaErrorNotSupported when the shapes or the format do not fit (the caller then uses the
+// mma.sync kernel of moe_tc.cu).
 cudaError_t launch_moe_layer_umma(int fmt, int fc, const bf16* x, const int* list, const uint8_t* w, const void* sc,
                                   bf16* h_out, float* part_out, int P, int R, int E, int e_end, int K, int rows_pg,
-                                  const LaunchCfg& cfg) {
+                                  const LaunchCfg& cfg, int split) {
   if (fmt != kFmtQ4 && fmt != kFmtIq2N) return cudaErrorNotSupported;
   // the activation rows (8 x K / 8 pieces of 16 bytes) are permuted through registers
   if (rows_pg % kTileRows || K % kKStep || K > kMaxXPieces * kDecW * 32 || P > 128) return cudaErrorNotSupported;
@@ -607,6 +653,11 @@ cudaError_t launch_moe_layer_umma(int fmt, int fc, const bf16* x, const int* lis
   p.sc = static_cast<const uint8_t*>(sc);
   p.h_out = h_out;
   p.part_out = part_out;
+  // fc1 zeroes the listed pairs' rows of fc2's output [P, 1024] (16-byte aligned) so that fc2
+  // may split tiles
+  p.zero_cols = 1024;
+  if (fc == 1 && part_out != nullptr && (reinterpret_cast<uintptr_t>(part_out) & 15)) return cudaErrorInvalidValue;
+  p.split = fc == 2 ? split : 0;
   p.P = P;
   p.R = R;
   p.K = K;
