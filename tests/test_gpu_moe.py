@@ -133,6 +133,21 @@ def test_moe_verify_config_r8(iq2):
     _check_moe("MoeVerify", [z, idx, w, ex["fc1_w"], ex["fc1_s"], ex["fc2_w"], ex["fc2_s"]], 8, iq2, on_device=True)
 
 
+@pytest.mark.parametrize("uniq", [19, 23])
+@pytest.mark.parametrize("iq2", [0, 2])
+def test_moe_verify_split_fc2_tiles(uniq, iq2):
+    # fc2 has 8 tiles of 128 rows per expert: 19 experts give 152 tiles for 148 SMs, so almost
+    # every tile is split between two CTAs at a K-segment boundary (23: 184 tiles, other cuts)
+    R, topk, E, I = 8, 3, 32, 2304
+    ex = W.moe_experts(E=E, I=I, iq2=iq2, seed=uniq)
+    picks = list(range(uniq)) + [(5 * j) % uniq for j in range(R * topk - uniq)]
+    idx = torch.tensor(picks, dtype=torch.int32).reshape(R, topk)
+    w = torch.rand(R, topk, generator=torch.Generator().manual_seed(uniq))
+    z = W.moe_latent(R=R, seed=uniq)
+    _check_moe("MoeVerify", [z, idx.to(DEV), w.to(DEV), ex["fc1_w"], ex["fc1_s"], ex["fc2_w"], ex["fc2_s"]], topk,
+               iq2, on_device=True)
+
+
 @pytest.mark.parametrize("R,E,I,topk", [(2, 24, 256, 3), (5, 40, 512, 4), (8, 12, 256, 6), (8, 64, 768, 8)])
 @pytest.mark.parametrize("iq2", [0, 1, 2])
 def test_moe_verify_small(R, E, I, topk, iq2):
