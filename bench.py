@@ -167,6 +167,35 @@ def _moe_workload(op_name, R, iq2=0, E=304, I=2304, topk=8):
     return build
 
 
+def _relu2_workload(R, C):
+    """Relu2 over x bf16 [R, C]: 2 bytes read and 2 written per element (an HBM stream)."""
+    from nemotron_ops_b200 import ops
+
+    def build(device, copies):
+        g = torch.Generator(device=device).manual_seed(0)
+        xs = [(torch.randn(R, C, generator=g, device=device) * 3).to(torch.bfloat16) for _ in range(copies)]
+        nbytes = 2 * R * C * 2
+        calls = [(lambda x=x: ops.Relu2(x)) for x in xs]
+        pin = str(device) != "cpu"
+        xh = xs[0].cpu().pin_memory() if pin else xs[0]
+        yh = torch.empty(R, C, dtype=torch.bfloat16).pin_memory() if pin else None
+        xd = torch.empty_like(xs[0])
+
+        def e2e(i):
+            xd.copy_(xh, non_blocking=True)
+            yh.copy_(ops.Relu2(xd), non_blocking=True)
+
+        def cpu(sample_rows):
+            import oracle as O
+            rows = max(1, min(R, sample_rows))
+            O.relu2(xs[0][:rows].cpu())
+            return nbytes * rows / R
+
+        return dict(calls=calls, bytes=nbytes, kernels=1, h2d=R * C * 2, d2h=R * C * 2, e2e=e2e, cpu=cpu,
+                    cpu_sample=1, dtype="f32", kernel="relu2_kernel")
+    return build
+
+
 WORKLOADS = {
     "nvfp4_r1": ("Nvfp4Gemv R=1 K=8192 N=4096 (configs[1])", _gemv_workload("nvfp4", 1, 4096, 8192)),
     "nvfp4_r8": ("Nvfp4Gemv R=8 K=8192 N=4096 (configs[1])", _gemv_workload("nvfp4", 8, 4096, 8192)),
@@ -180,6 +209,7 @@ WORKLOADS = {
     "moe_decode_r1": ("MoeDecode R=1 E=304 k=8 I=2304 (configs[3])", _moe_workload("MoeDecode", 1)),
     "moe_verify_r8": ("MoeVerify int4 R=8 E=304 k=8 I=2304 (configs[4])", _moe_workload("MoeVerify", 8)),
     "moe_verify_iq2n_r8": ("MoeVerify iq2=2 R=8 E=304 k=8 I=2304 (configs[4])", _moe_workload("MoeVerify", 8, iq2=2)),
+    "relu2": ("Relu2 x bf16 [8, 4194304] (not a BASELINE config; HBM stream)", _relu2_workload(8, 4194304)),
 }
 
 

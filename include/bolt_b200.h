@@ -195,6 +195,13 @@ BOLT_API int bolt_moe_verify_noalloc(const void* z, const int64_t* z_shape, int 
                                      int64_t iq2, void* out, void* stream);
 
 /*
+ * Relu2 (replaces Relu2State::ComputeV2, src/bolt_ops.cu:630-646; kernel :624-629).
+ *   x bf16 of any shape (x_shape[x_rank]) -> y bf16 of the same shape,
+ *   y = bf16(max(x, 0)^2) with the square in fp32 (a NaN input gives 0, as fmaxf there).
+ */
+BOLT_API int bolt_relu2(const void* x, const int64_t* x_shape, int x_rank, void* y, void* stream);
+
+/*
  * out[i] = bf16(in[i]) for n f32 values (the cast after the shard all-reduce).
  */
 BOLT_API int bolt_f32_to_bf16(const void* in, void* out, int64_t n, void* stream);

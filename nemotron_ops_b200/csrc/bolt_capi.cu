@@ -343,6 +343,18 @@ int bolt_moe_verify_shard(const void* z, const int64_t* z_shape, int z_rank, con
                          e_begin, e_end, true, out, h, part, meta, out_partial, stream);
 }
 
+int bolt_relu2(const void* x, const int64_t* x_shape, int x_rank, void* y, void* stream) {
+  return guarded([&] {
+    const Shape xs{x_shape, x_rank};
+    require(x_rank >= 0 && (x_rank == 0 || x_shape != nullptr), "Relu2: bad shape");
+    for (int i = 0; i < x_rank; ++i) require(x_shape[i] >= 0, "Relu2: negative dimension");
+    const int64_t n = xs.count();
+    if (n == 0) return;
+    require(x != nullptr && y != nullptr, "Relu2: null buffer");
+    check_launch(launch_relu2(static_cast<const bf16*>(x), static_cast<bf16*>(y), n, make_cfg(stream)));
+  });
+}
+
 int bolt_f32_to_bf16(const void* in, void* out, int64_t n, void* stream) {
   return guarded([&] {
     require(n >= 0, "bolt_f32_to_bf16: negative size");

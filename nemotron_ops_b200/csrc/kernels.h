@@ -57,6 +57,10 @@ cudaError_t launch_gemv_mma(int fmt, const bf16* x, int R, const uint8_t* w, con
 cudaError_t launch_dequant(int fmt, int exact, const uint8_t* w, const void* sc, int64_t N, int K, float* out,
                            const LaunchCfg& cfg);
 
+// ---- Relu2 -----------------------------------------------------------------------------
+// y = bf16(max(x, 0)^2) over n bf16 values.
+cudaError_t launch_relu2(const bf16* x, bf16* y, int64_t n, const LaunchCfg& cfg);
+
 // ---- MoE -------------------------------------------------------------------------------
 cudaError_t launch_moe_route(const bf16* x, const bf16* gate_w, const float* bias, int R, int K, int E, int topk,
                              float scale, int* idx, float* w, float* scores, const LaunchCfg& cfg);

@@ -202,6 +202,17 @@ def moe_decode_shard(z, idx, w, fc1_w, fc1_s, fc2_w, fc2_s, topk: int, e_begin: 
     return out_partial, h, part
 
 
+def Relu2(x):
+    """Returns y bf16 of x's shape, bf16(max(x, 0)^2) (src/bolt_ops.cu:624-646)."""
+    _need(x)
+    if x.dtype != torch.bfloat16:
+        raise RuntimeError("Relu2 takes bf16")
+    y = torch.empty_like(x)
+    xs, _keep = shape_arg(x.shape)
+    _check(lib().bolt_relu2(_ptr(x), xs, x.dim(), _ptr(y), _stream(x)))
+    return y
+
+
 def f32_to_bf16(t, out=None):
     _need(t)
     if out is None:

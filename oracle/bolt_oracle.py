@@ -38,7 +38,7 @@ import torch
 __all__ = [
     "FP4_VALUES", "IQ2_LUT_BF16", "iq2xxs_grid", "bf16_round", "unpack_nibbles",
     "q8_dequant", "q4_dequant", "nvfp4_dequant", "iq2_lut_dequant", "iq2n_dequant",
-    "iq2n_dequant_gguf_style", "gemv_contract", "q8_gemv", "q4_gemv", "nvfp4_gemv",
+    "iq2n_dequant_gguf_style", "gemv_contract", "q8_gemv", "q4_gemv", "nvfp4_gemv", "relu2",
     "moe_route", "route_min_gap", "moe_group_meta", "moe_decode", "moe_verify", "moe_combine", "moe_verify_partial",
     "moe_decode_partial",
     "moe_expert_weights",
@@ -220,6 +220,17 @@ def nvfp4_gemv(x, w, w_scale, g, fp32: bool = False):
     """Nvfp4Gemv (src/bolt_ops.cu:1259-1306): y = bf16(g * x @ (e2m1 * e4m3)^T)."""
     gs = float(torch.as_tensor(g).reshape(-1)[0])
     return gemv_contract(x, nvfp4_dequant(w, w_scale), gscale=gs, fp32=fp32)
+
+
+# ----------------------------------------------------------------------------------------
+# Relu2
+# ----------------------------------------------------------------------------------------
+def relu2(x: torch.Tensor) -> torch.Tensor:
+    """bf16(max(x, 0)^2), square in fp32 (Relu2Kernel, src/bolt_ops.cu:624-629; the reference
+    test's expression tests/test_bolt_ops.py:102).  max follows the kernel's fmaxf: NaN -> 0."""
+    xf = x.float()
+    r = torch.where(xf > 0, xf, torch.zeros_like(xf))
+    return (r * r).to(torch.bfloat16)
 
 
 # ----------------------------------------------------------------------------------------

@@ -119,3 +119,12 @@ def test_dequant_validation():
     assert lib.bolt_dequant(7, 0, NULL, NULL, 4, 64, NULL, NULL) == 1
     assert _lib.last_error() == "bolt_dequant: unknown format"
     assert lib.bolt_dequant(2, 1, NULL, NULL, 4, 64, NULL, NULL) == 1
+
+
+def test_relu2_validation_and_empty():
+    lib = _lib.lib()
+    xs, k1 = _sh(3, -1)
+    assert lib.bolt_relu2(NULL, xs, 2, NULL, NULL) != 0
+    assert "Relu2: negative dimension" in _lib.last_error()
+    xs, k2 = _sh(0, 1000)  # nothing to do: no device work, no pointer needed
+    assert lib.bolt_relu2(NULL, xs, 2, NULL, NULL) == 0

@@ -135,3 +135,13 @@ def test_route_topk_exceeds_experts():
     gw = torch.randn(3, 256).bfloat16()
     idx, w, s = O.moe_route(x, gw, torch.zeros(3), 5, 1.0)
     assert idx[0, 3:].tolist() == [-1, -1] and w[0, 3:].tolist() == [0.0, 0.0]
+
+
+def test_relu2_oracle():
+    c = load("relu2")
+    (x,) = c.inputs
+    assert torch.equal(O.relu2(x).float(), c.ref)  # the reference test demands equality
+    # the kernel's fmaxf: NaN and -0 give +0; overflow of the fp32 square gives inf
+    s = torch.tensor([float("nan"), -0.0, 0.0, -1e30, 1e30, float("inf"), -float("inf"), 1e-30, 2.5],
+                     dtype=torch.bfloat16)
+    assert O.relu2(s).float().tolist()[:8] == [0.0, 0.0, 0.0, 0.0, float("inf"), float("inf"), 0.0, 0.0]
