@@ -196,6 +196,57 @@ def _relu2_workload(R, C):
     return build
 
 
+def _mamba_workload(R, verify, heads=128, ng=8):
+    """MambaStep (verify: MambaVerify from row 3 of R-row state buffers) at the reference test's
+    size (tests/test_bolt_ops.py:264): the fp32 SSM state dominates the bytes."""
+    from nemotron_ops_b200 import ops
+
+    def build(device, copies):
+        g = torch.Generator(device=device).manual_seed(0)
+        di, rows = heads * 64, (R if verify else 1)
+        cd = di + 2 * ng * 128
+
+        def rnd(*shape, scale=1.0):
+            return torch.randn(*shape, generator=g, device=device) * scale
+
+        shared = [(rnd(cd, 1, 4, scale=0.3)).bfloat16(), rnd(cd, scale=0.1).bfloat16(), rnd(heads, scale=0.3),
+                  -torch.rand(heads, generator=g, device=device) * 4 - 0.1, rnd(heads),
+                  torch.rand(di, generator=g, device=device) + 0.5]
+        sets = [[rnd(R, di + cd + heads, scale=0.7).bfloat16(), rnd(rows, cd, 3, scale=0.5).bfloat16(),
+                 rnd(rows, heads, 128, 64, scale=0.1)] for _ in range(copies)]
+        sel = torch.tensor([3 % rows], dtype=torch.int32, device=device)
+        attrs = dict(heads=heads, head_dim=64, d_state=128, n_groups=ng, epsilon=1e-5, time_step_min=0.001)
+
+        def op(s3):
+            if verify:
+                return ops.MambaVerify(*s3, *shared, sel, **attrs)
+            return ops.MambaStep(*s3, *shared, **attrs)
+
+        state_rows_out = R if verify else 1
+        nbytes = (R * (di + cd + heads) * 2 + cd * 3 * 2 + cd * 4 * 2 + cd * 2 + heads * 128 * 64 * 4 +
+                  3 * heads * 4 + di * 4 + R * di * 2 + state_rows_out * (cd * 3 * 2 + heads * 128 * 64 * 4) +
+                  R * cd * 2 + R * di * 4)
+        calls = [(lambda s3=s3: op(s3)) for s3 in sets]
+        pin = str(device) != "cpu"
+        ph = sets[0][0].cpu().pin_memory() if pin else sets[0][0]
+        yh = torch.empty(R, di, dtype=torch.bfloat16).pin_memory() if pin else None
+        pd = torch.empty_like(sets[0][0])
+
+        def e2e(i):
+            pd.copy_(ph, non_blocking=True)
+            yh.copy_(op([pd, sets[i][1], sets[i][2]])[0], non_blocking=True)
+
+        def cpu(_sample):
+            import oracle as O
+            c = [t.cpu() for t in sets[0] + shared]
+            O.mamba_step(*c, **attrs, sel=(3 % rows) if verify else None)
+            return nbytes
+
+        return dict(calls=calls, bytes=nbytes, kernels=3, h2d=R * (di + cd + heads) * 2, d2h=R * di * 2, e2e=e2e,
+                    cpu=cpu, cpu_sample=1, dtype="f32", kernel="mamba_ssm_kernel")
+    return build
+
+
 WORKLOADS = {
     "nvfp4_r1": ("Nvfp4Gemv R=1 K=8192 N=4096 (configs[1])", _gemv_workload("nvfp4", 1, 4096, 8192)),
     "nvfp4_r8": ("Nvfp4Gemv R=8 K=8192 N=4096 (configs[1])", _gemv_workload("nvfp4", 8, 4096, 8192)),
@@ -210,6 +261,10 @@ WORKLOADS = {
     "moe_verify_r8": ("MoeVerify int4 R=8 E=304 k=8 I=2304 (configs[4])", _moe_workload("MoeVerify", 8)),
     "moe_verify_iq2n_r8": ("MoeVerify iq2=2 R=8 E=304 k=8 I=2304 (configs[4])", _moe_workload("MoeVerify", 8, iq2=2)),
     "relu2": ("Relu2 x bf16 [8, 4194304] (not a BASELINE config; HBM stream)", _relu2_workload(8, 4194304)),
+    "mamba_step_r1": ("MambaStep R=1 heads=128 ng=8 (not a BASELINE config; reference test size)",
+                      _mamba_workload(1, False)),
+    "mamba_verify_r8": ("MambaVerify R=8 sel=3 heads=128 ng=8 (not a BASELINE config; reference test size)",
+                        _mamba_workload(8, True)),
 }
 
 

@@ -65,7 +65,8 @@ BOLT_API int bolt_set_launch_options(int pdl, int early_weights, int64_t smem_bu
  * Reads and clears the device status word of the current device (synchronises the device).
  * Nonzero bits mean a kernel gave up a bounded wait (2 s) and returned without finishing
  * (bits 0-2, 4); bit 3 means a MoE expert id outside [0, E) was skipped; bit 5 means a
- * kernel found its shared-memory carve-out misaligned and returned without computing.
+ * kernel found its shared-memory carve-out misaligned and returned without computing; bit 6
+ * means a MambaVerify `sel` row lay outside its state buffers and nothing was written.
  * No counterpart in the reference.
  */
 BOLT_API int bolt_get_device_status(unsigned* status);
@@ -193,6 +194,38 @@ BOLT_API int bolt_moe_verify_noalloc(const void* z, const int64_t* z_shape, int 
                                      const void* w, const void* fc1_w, const int64_t* fc1_w_shape, int fc1_w_rank,
                                      const void* fc1_s, const void* fc2_w, const void* fc2_s, int64_t topk,
                                      int64_t iq2, void* out, void* stream);
+
+/*
+ * MambaStep (replaces MambaStepState::ComputeV2, src/bolt_ops.cu:299-357; kernels :63-297).
+ * Attributes heads, head_dim (= 64), d_state (= 128), n_groups, epsilon, time_step_min.
+ * di = heads * head_dim, cd = di + 2 * n_groups * d_state.
+ *   proj        bf16 [R, di + cd + heads]   rows [gate | xBC | dt], 1 <= R <= 16
+ *   conv_state  bf16 [rows, cd, 3];  ssm_state f32 [rows, heads, d_state, head_dim]
+ *   conv_w bf16 [cd, 1, 4]; conv_b bf16 [cd]; dt_bias, a_neg, d_skip f32 [heads]; norm_w f32 [di]
+ * Outputs: y bf16 [R, di]; conv_state_out / ssm_state_out shaped like the inputs (row 0 = the
+ * state after the R tokens, starting from row 0); xbc_act bf16 [R, cd]; ypre f32 [R, di].
+ */
+BOLT_API int bolt_mamba_step(const void* proj, const int64_t* proj_shape, int proj_rank, const void* conv_state,
+                             const int64_t* conv_shape, int conv_rank, const void* ssm_state, const int64_t* ssm_shape,
+                             int ssm_rank, const void* conv_w, const void* conv_b, const void* dt_bias,
+                             const void* a_neg, const void* d_skip, const void* norm_w, int64_t heads,
+                             int64_t head_dim, int64_t d_state, int64_t n_groups, float epsilon, float time_step_min,
+                             void* y, void* conv_state_out, void* ssm_state_out, void* xbc_act, void* ypre,
+                             void* stream);
+
+/*
+ * MambaVerify (the reference's MambaVerifyOp: MambaStepState in verify mode, src/bolt_ops.cu:303,
+ * :316-330).  As bolt_mamba_step, plus sel i32 [1] (device): the tokens start from state row
+ * *sel and the state after token r is written to row r (needs rows >= R).  A sel outside
+ * [0, rows) writes nothing and sets bit 6 of the device status word.
+ */
+BOLT_API int bolt_mamba_verify(const void* proj, const int64_t* proj_shape, int proj_rank, const void* conv_state,
+                               const int64_t* conv_shape, int conv_rank, const void* ssm_state,
+                               const int64_t* ssm_shape, int ssm_rank, const void* conv_w, const void* conv_b,
+                               const void* dt_bias, const void* a_neg, const void* d_skip, const void* norm_w,
+                               const void* sel, int64_t heads, int64_t head_dim, int64_t d_state, int64_t n_groups,
+                               float epsilon, float time_step_min, void* y, void* conv_state_out,
+                               void* ssm_state_out, void* xbc_act, void* ypre, void* stream);
 
 /*
  * Relu2 (replaces Relu2State::ComputeV2, src/bolt_ops.cu:630-646; kernel :624-629).

@@ -10,6 +10,7 @@ _P = ctypes.c_void_p
 _S = ctypes.POINTER(ctypes.c_int64)
 _I = ctypes.c_int
 _L = ctypes.c_int64
+_F = ctypes.c_float
 
 # name -> (restype, argtypes); kept in the order of include/bolt_b200.h
 SIGNATURES = {
@@ -27,6 +28,10 @@ SIGNATURES = {
     "bolt_moe_verify_shard": (_I, [_P, _S, _I, _P, _P, _P, _S, _I, _P, _P, _P, _L, _L, _L, _L, _P, _P, _P, _P, _P,
                                    _P]),
     "bolt_moe_decode_shard": (_I, [_P, _S, _I, _P, _P, _P, _S, _I, _P, _P, _P, _L, _L, _L, _P, _P, _P, _P, _P]),
+    "bolt_mamba_step": (_I, [_P, _S, _I, _P, _S, _I, _P, _S, _I, _P, _P, _P, _P, _P, _P, _L, _L, _L, _L, _F, _F,
+                             _P, _P, _P, _P, _P, _P]),
+    "bolt_mamba_verify": (_I, [_P, _S, _I, _P, _S, _I, _P, _S, _I, _P, _P, _P, _P, _P, _P, _P, _L, _L, _L, _L, _F,
+                               _F, _P, _P, _P, _P, _P, _P]),
     "bolt_relu2": (_I, [_P, _S, _I, _P, _P]),
     "bolt_f32_to_bf16": (_I, [_P, _P, _L, _P]),
     "bolt_dequant": (_I, [_I, _I, _P, _P, _L, _L, _P, _P]),

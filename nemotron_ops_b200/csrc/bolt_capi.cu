@@ -343,6 +343,90 @@ int bolt_moe_verify_shard(const void* z, const int64_t* z_shape, int z_rank, con
                          e_begin, e_end, true, out, h, part, meta, out_partial, stream);
 }
 
+namespace {
+int mamba_impl(const void* proj, const int64_t* proj_shape, int proj_rank, const void* conv_state,
+               const int64_t* conv_shape, int conv_rank, const void* ssm_state, const int64_t* ssm_shape, int ssm_rank,
+               const void* conv_w, const void* conv_b, const void* dt_bias, const void* a_neg, const void* d_skip,
+               const void* norm_w, const void* sel, int64_t heads, int64_t head_dim, int64_t d_state,
+               int64_t n_groups, float epsilon, float time_step_min, void* y, void* conv_out, void* ssm_out,
+               void* xbc_act, void* ypre, void* stream) {
+  return guarded([&] {
+    const bool verify = sel != nullptr;
+    // src/bolt_ops.cu:311 (attributes), :316-322 (rows, proj width), :325 (verify rows)
+    if (head_dim != 64 || d_state != 128)
+      throw std::invalid_argument("MambaStep: only head_dim=64, d_state=128 are implemented");
+    const Shape ps{proj_shape, proj_rank}, cs{conv_shape, conv_rank}, ss{ssm_shape, ssm_rank};
+    const int64_t R = ps.dim(0);
+    require(R >= 1 && R <= 16, "MambaStep: rows must be in [1,16]");
+    require(heads >= 1 && n_groups >= 1 && heads % n_groups == 0, "MambaStep: heads must be a multiple of n_groups");
+    const int64_t di = heads * head_dim, cd = di + 2 * n_groups * d_state, stride = di + cd + heads;
+    require(ps.dim(1) == stride, "MambaStep: bad proj width");
+    if (verify) require(cs.dim(0) >= R, "MambaVerify: state buffer needs >= R rows");
+    // shapes the reference takes on trust
+    require(conv_rank == 3 && cs.dim(0) >= 1 && cs.dim(1) == cd && cs.dim(2) == 3,
+            "MambaStep: conv state must be [rows, conv_dim, 3]");
+    require(ssm_rank == 4 && ss.dim(0) == cs.dim(0) && ss.dim(1) == heads && ss.dim(2) == d_state &&
+                ss.dim(3) == head_dim,
+            "MambaStep: ssm state must be [rows, heads, d_state, head_dim] with the conv state's rows");
+    MambaParams p{};
+    p.proj = static_cast<const bf16*>(proj);
+    p.conv_in = static_cast<const bf16*>(conv_state);
+    p.conv_w = static_cast<const bf16*>(conv_w);
+    p.conv_b = static_cast<const bf16*>(conv_b);
+    p.ssm_in = static_cast<const float*>(ssm_state);
+    p.dt_bias = static_cast<const float*>(dt_bias);
+    p.a_neg = static_cast<const float*>(a_neg);
+    p.d_skip = static_cast<const float*>(d_skip);
+    p.norm_w = static_cast<const float*>(norm_w);
+    p.sel = static_cast<const int*>(sel);
+    p.y = static_cast<bf16*>(y);
+    p.conv_out = static_cast<bf16*>(conv_out);
+    p.ssm_out = static_cast<float*>(ssm_out);
+    p.xbc = static_cast<bf16*>(xbc_act);
+    p.ypre = static_cast<float*>(ypre);
+    p.R = static_cast<int>(R);
+    p.rows = static_cast<int>(cs.dim(0));
+    p.stride = static_cast<int>(stride);
+    p.di = static_cast<int>(di);
+    p.cd = static_cast<int>(cd);
+    p.heads = static_cast<int>(heads);
+    p.hd = static_cast<int>(head_dim);
+    p.ds = static_cast<int>(d_state);
+    p.ng = static_cast<int>(n_groups);
+    p.hpg = static_cast<int>(heads / n_groups);
+    p.eps = epsilon;
+    p.tmin = time_step_min;
+    check_launch(launch_mamba(p, make_cfg(stream)));
+  });
+}
+}  // namespace
+
+int bolt_mamba_step(const void* proj, const int64_t* proj_shape, int proj_rank, const void* conv_state,
+                    const int64_t* conv_shape, int conv_rank, const void* ssm_state, const int64_t* ssm_shape,
+                    int ssm_rank, const void* conv_w, const void* conv_b, const void* dt_bias, const void* a_neg,
+                    const void* d_skip, const void* norm_w, int64_t heads, int64_t head_dim, int64_t d_state,
+                    int64_t n_groups, float epsilon, float time_step_min, void* y, void* conv_state_out,
+                    void* ssm_state_out, void* xbc_act, void* ypre, void* stream) {
+  return mamba_impl(proj, proj_shape, proj_rank, conv_state, conv_shape, conv_rank, ssm_state, ssm_shape, ssm_rank,
+                    conv_w, conv_b, dt_bias, a_neg, d_skip, norm_w, nullptr, heads, head_dim, d_state, n_groups,
+                    epsilon, time_step_min, y, conv_state_out, ssm_state_out, xbc_act, ypre, stream);
+}
+
+int bolt_mamba_verify(const void* proj, const int64_t* proj_shape, int proj_rank, const void* conv_state,
+                      const int64_t* conv_shape, int conv_rank, const void* ssm_state, const int64_t* ssm_shape,
+                      int ssm_rank, const void* conv_w, const void* conv_b, const void* dt_bias, const void* a_neg,
+                      const void* d_skip, const void* norm_w, const void* sel, int64_t heads, int64_t head_dim,
+                      int64_t d_state, int64_t n_groups, float epsilon, float time_step_min, void* y,
+                      void* conv_state_out, void* ssm_state_out, void* xbc_act, void* ypre, void* stream) {
+  if (sel == nullptr) {
+    g_last_error = "MambaVerify: sel must not be null";
+    return BOLT_FAIL;
+  }
+  return mamba_impl(proj, proj_shape, proj_rank, conv_state, conv_shape, conv_rank, ssm_state, ssm_shape, ssm_rank,
+                    conv_w, conv_b, dt_bias, a_neg, d_skip, norm_w, sel, heads, head_dim, d_state, n_groups, epsilon,
+                    time_step_min, y, conv_state_out, ssm_state_out, xbc_act, ypre, stream);
+}
+
 int bolt_relu2(const void* x, const int64_t* x_shape, int x_rank, void* y, void* stream) {
   return guarded([&] {
     const Shape xs{x_shape, x_rank};

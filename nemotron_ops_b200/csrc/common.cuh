@@ -30,6 +30,7 @@ enum StatusBits : unsigned {
   kStatusBadExpert = 1u << 3,   // an expert id outside [0, E) was skipped
   kStatusGridWait = 1u << 4,    // a cross-CTA wait timed out
   kStatusSmemAlign = 1u << 5,   // the shared-memory carve-out was not aligned as required
+  kStatusBadRow = 1u << 6,      // a MambaVerify state row (sel) outside the state buffer: nothing written
 };
 
 extern __device__ unsigned g_status;

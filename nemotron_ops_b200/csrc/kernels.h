@@ -61,6 +61,30 @@ cudaError_t launch_dequant(int fmt, int exact, const uint8_t* w, const void* sc,
 // y = bf16(max(x, 0)^2) over n bf16 values.
 cudaError_t launch_relu2(const bf16* x, bf16* y, int64_t n, const LaunchCfg& cfg);
 
+// ---- Mamba ---------------------------------------------------------------------------
+// One MambaStep (sel == null: state row 0 in and out) or MambaVerify (start from row *sel,
+// the state after token r to row r) over R tokens; see mamba.cu.
+struct MambaParams {
+  const bf16* proj;      // [R, stride], stride = di + cd + heads
+  const bf16* conv_in;   // [rows, cd, 3]
+  const bf16* conv_w;    // [cd, 1, 4]
+  const bf16* conv_b;    // [cd]
+  const float* ssm_in;   // [rows, heads, ds, hd]
+  const float* dt_bias;  // [heads]
+  const float* a_neg;    // [heads]
+  const float* d_skip;   // [heads]
+  const float* norm_w;   // [di]
+  const int* sel;        // device pointer to the start row (MambaVerify) or null (MambaStep)
+  bf16* y;               // [R, di]
+  bf16* conv_out;        // like conv_in
+  float* ssm_out;        // like ssm_in
+  bf16* xbc;             // [R, cd]
+  float* ypre;           // [R, di]
+  int R, rows, stride, di, cd, heads, hd, ds, ng, hpg;
+  float eps, tmin;
+};
+cudaError_t launch_mamba(const MambaParams& p, const LaunchCfg& cfg);
+
 // ---- MoE -------------------------------------------------------------------------------
 cudaError_t launch_moe_route(const bf16* x, const bf16* gate_w, const float* bias, int R, int K, int E, int topk,
                              float scale, int* idx, float* w, float* scores, const LaunchCfg& cfg);

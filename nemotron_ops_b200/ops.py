@@ -202,6 +202,49 @@ def moe_decode_shard(z, idx, w, fc1_w, fc1_s, fc2_w, fc2_s, topk: int, e_begin: 
     return out_partial, h, part
 
 
+def _mamba(proj, conv_state, ssm_state, conv_w, conv_b, dt_bias, a_neg, d_skip, norm_w, sel, heads, head_dim,
+           d_state, n_groups, epsilon, time_step_min):
+    tensors = [proj, conv_state, ssm_state, conv_w, conv_b, dt_bias, a_neg, d_skip, norm_w]
+    _need(*tensors + ([sel] if sel is not None else []))
+    R = proj.shape[0]
+    di = heads * head_dim
+    cd = di + 2 * n_groups * d_state
+    dev = proj.device
+    y = torch.empty(R, di, dtype=torch.bfloat16, device=dev)
+    conv_out = torch.empty_like(conv_state)
+    ssm_out = torch.empty_like(ssm_state)
+    xbc = torch.empty(R, cd, dtype=torch.bfloat16, device=dev)
+    ypre = torch.empty(R, di, dtype=torch.float32, device=dev)
+    ps, _k1 = shape_arg(proj.shape)
+    cs, _k2 = shape_arg(conv_state.shape)
+    ss, _k3 = shape_arg(ssm_state.shape)
+    head = [_ptr(proj), ps, proj.dim(), _ptr(conv_state), cs, conv_state.dim(), _ptr(ssm_state), ss,
+            ssm_state.dim()] + [_ptr(t) for t in tensors[3:]]
+    tail = [int(heads), int(head_dim), int(d_state), int(n_groups), float(epsilon), float(time_step_min), _ptr(y),
+            _ptr(conv_out), _ptr(ssm_out), _ptr(xbc), _ptr(ypre), _stream(proj)]
+    if sel is None:
+        _check(lib().bolt_mamba_step(*head, *tail))
+    else:
+        _check(lib().bolt_mamba_verify(*head, _ptr(sel), *tail))
+    return y, conv_out, ssm_out, xbc, ypre
+
+
+def MambaStep(proj, conv_state, ssm_state, conv_w, conv_b, dt_bias, a_neg, d_skip, norm_w, heads: int,
+              head_dim: int, d_state: int, n_groups: int, epsilon: float, time_step_min: float):
+    """Returns (y bf16 [R, di], conv_state_out, ssm_state_out, xbc_act bf16 [R, cd], ypre f32 [R, di])
+    (src/bolt_ops.cu:299-357); the state outputs are shaped like the inputs, row 0 written."""
+    return _mamba(proj, conv_state, ssm_state, conv_w, conv_b, dt_bias, a_neg, d_skip, norm_w, None, heads, head_dim,
+                  d_state, n_groups, epsilon, time_step_min)
+
+
+def MambaVerify(proj, conv_state, ssm_state, conv_w, conv_b, dt_bias, a_neg, d_skip, norm_w, sel, heads: int,
+                head_dim: int, d_state: int, n_groups: int, epsilon: float, time_step_min: float):
+    """As MambaStep from state row sel (i32 [1] on the device); the state after token r goes to
+    row r of the state outputs (rows >= R only are left unwritten)."""
+    return _mamba(proj, conv_state, ssm_state, conv_w, conv_b, dt_bias, a_neg, d_skip, norm_w, sel, heads, head_dim,
+                  d_state, n_groups, epsilon, time_step_min)
+
+
 def Relu2(x):
     """Returns y bf16 of x's shape, bf16(max(x, 0)^2) (src/bolt_ops.cu:624-646)."""
     _need(x)

@@ -8,7 +8,8 @@ tianleiwu/nemotron_ops):
 
 * the torch references of ``tests/test_bolt_ops.py`` (the reference's own oracle):
   NVFP4 ``:68,76-78``, Q8/Q4 ``:88-95``, MoeRoute ``:115-119``, the MoE rounding
-  points ``:145-150``, IQ2 LUT codes ``:157-180``, native IQ2_XXS ``:211-243``;
+  points ``:145-150``, IQ2 LUT codes ``:157-180``, native IQ2_XXS ``:211-243``, Relu2
+  ``:99-104`` and MambaStep ``:281-303``;
 * the kernel rounding contract of ``src/bolt_ops.cu`` that the tests only check to a
   tolerance: ``DequantRow`` ``:860-919`` (weights of the tensor-core path are
   rounded to bf16), the exact fp32 weights of the SIMT kernels ``:480-494,1315-1326``,
@@ -38,7 +39,7 @@ import torch
 __all__ = [
     "FP4_VALUES", "IQ2_LUT_BF16", "iq2xxs_grid", "bf16_round", "unpack_nibbles",
     "q8_dequant", "q4_dequant", "nvfp4_dequant", "iq2_lut_dequant", "iq2n_dequant",
-    "iq2n_dequant_gguf_style", "gemv_contract", "q8_gemv", "q4_gemv", "nvfp4_gemv", "relu2",
+    "iq2n_dequant_gguf_style", "gemv_contract", "q8_gemv", "q4_gemv", "nvfp4_gemv", "relu2", "mamba_step",
     "moe_route", "route_min_gap", "moe_group_meta", "moe_decode", "moe_verify", "moe_combine", "moe_verify_partial",
     "moe_decode_partial",
     "moe_expert_weights",
@@ -220,6 +221,50 @@ def nvfp4_gemv(x, w, w_scale, g, fp32: bool = False):
     """Nvfp4Gemv (src/bolt_ops.cu:1259-1306): y = bf16(g * x @ (e2m1 * e4m3)^T)."""
     gs = float(torch.as_tensor(g).reshape(-1)[0])
     return gemv_contract(x, nvfp4_dequant(w, w_scale), gscale=gs, fp32=fp32)
+
+
+# ----------------------------------------------------------------------------------------
+# MambaStep / MambaVerify
+# ----------------------------------------------------------------------------------------
+def mamba_step(proj, conv_state, ssm_state, conv_w, conv_b, dt_bias, a_neg, d_skip, norm_w, heads: int,
+               head_dim: int, d_state: int, n_groups: int, epsilon: float, time_step_min: float, sel=None):
+    """One Mamba-2 step over the R rows of proj, starting from state row ``sel`` (0 when None).
+
+    Restates the reference test's torch reference (tests/test_bolt_ops.py:281-303) with the
+    kernels' rounding points (src/bolt_ops.cu:92, conv output rounded to bf16 before the SSM).
+    Returns (y f32 [R, di] before the output's bf16 rounding, conv states bf16 [R, cd, 3] and
+    ssm states f32 [R, heads, d_state, head_dim] after each token, xbc_act bf16 [R, cd],
+    ypre f32 [R, di]).
+    """
+    F = torch.nn.functional
+    R = proj.shape[0]
+    di = heads * head_dim
+    cd = di + 2 * n_groups * d_state
+    row = 0 if sel is None else int(sel)
+    gate, xbc, dt = proj.float().split([di, cd, heads], -1)
+    inp = torch.cat([conv_state[row].float().T, xbc], 0)  # [3 + R, cd]
+    cw = conv_w[:, 0, :].float().T                         # [4, cd]
+    conv = torch.stack([F.silu((inp[r:r + 4] * cw).sum(0) + conv_b.float()) for r in range(R)])
+    xbc_act = conv.to(torch.bfloat16)
+    conv_states = torch.stack([inp[r + 1:r + 4].T for r in range(R)]).to(torch.bfloat16)
+    xs, Bm, Cm = xbc_act.float().split([di, n_groups * d_state, n_groups * d_state], -1)
+    hpg = heads // n_groups
+    st = ssm_state[row].float().clone()
+    states, ys = [], []
+    for r in range(R):
+        dts = torch.clamp(F.softplus(dt[r] + dt_bias.float()), min=time_step_min)
+        dA = torch.exp(a_neg.float() * dts)
+        xh = xs[r].reshape(heads, head_dim)
+        Bh = Bm[r].reshape(n_groups, d_state).repeat_interleave(hpg, 0)
+        Ch = Cm[r].reshape(n_groups, d_state).repeat_interleave(hpg, 0)
+        st = st * dA[:, None, None] + (dts[:, None] * xh)[:, None, :] * Bh[:, :, None]
+        states.append(st.clone())
+        ys.append((st * Ch[:, :, None]).sum(1) + d_skip.float()[:, None] * xh)
+    ypre = torch.stack(ys).reshape(R, di)
+    g = (ypre * F.silu(gate)).reshape(R, n_groups, di // n_groups)
+    g = g * torch.rsqrt(g.pow(2).mean(-1, keepdim=True) + epsilon)
+    y = g.reshape(R, di) * norm_w.float()
+    return y, conv_states, torch.stack(states), xbc_act, ypre
 
 
 # ----------------------------------------------------------------------------------------

@@ -103,6 +103,12 @@ class Recorder:
             return [torch.zeros(R, k, dtype=torch.int32), torch.zeros(R, k), torch.zeros(R, E)]
         if op == "Relu2":
             return [torch.zeros_like(x)]
+        if op == "MambaStep":
+            R, heads, hd, ds, ng = x.shape[0], attrs["heads"], attrs["head_dim"], attrs["d_state"], attrs["n_groups"]
+            di = heads * hd
+            cd = di + 2 * ng * ds
+            return [torch.zeros(R, di, dtype=torch.bfloat16), torch.zeros_like(inputs[1][1]),
+                    torch.zeros_like(inputs[2][1]), torch.zeros(R, cd, dtype=torch.bfloat16), torch.zeros(R, di)]
         R = x.shape[0]
         return [torch.zeros(R, 1024, dtype=torch.bfloat16)]
 
@@ -118,7 +124,7 @@ def _to_np(t: torch.Tensor):
     return t.contiguous().numpy(), str(t.dtype).replace("torch.", "")
 
 
-def save_case(name, op, inputs, attrs, ref, deq=None, meta=None):
+def save_case(name, op, inputs, attrs, ref, deq=None, meta=None, extra=None):
     arrays, dtypes, names = {}, {}, []
     for n, t in inputs:
         a, dt = _to_np(t)
@@ -128,6 +134,8 @@ def save_case(name, op, inputs, attrs, ref, deq=None, meta=None):
     arrays["ref"] = ref.to(torch.float32).numpy()
     if deq is not None:
         arrays["gguf_deq"] = deq.to(torch.float32).numpy()
+    for k, t in (extra or {}).items():
+        arrays["ref_" + k] = t.to(torch.float32).numpy()
     info = {"op": op, "attrs": attrs, "inputs": names, "dtypes": dtypes, **(meta or {})}
     arrays["info"] = np.frombuffer(json.dumps(info).encode(), dtype=np.uint8)
     np.savez_compressed(os.path.join(HERE, name + ".npz"), **arrays)
@@ -166,6 +174,9 @@ CASES = [
     ("test_moe_iq2_native", dict(R=2, E=5, I=256, topk=3), "moe_verify_iq2n_r2"),
     ("test_moe_iq2_native", dict(R=8, E=3, I=256, topk=2), "moe_verify_iq2n_r8_shared"),
     ("test_relu2", dict(), "relu2"),  # the reference's own shape (3, 1000); unseeded there: seed 0 here
+    # MambaStep: 16 heads in 4 groups keep the fixtures small (the kernels' head_dim 64, d_state 128)
+    ("test_mamba", dict(R=1, heads=16, ng=4), "mamba_r1"),
+    ("test_mamba", dict(R=5, heads=16, ng=4), "mamba_r5"),
 ]
 
 
@@ -187,7 +198,9 @@ def main():
         assert len(calls) == 1 and refs, (name, len(calls), len(refs))
         op, inputs, attrs = calls[0]
         deq = deqs[0] if (deqs and op == "Q4Gemv") else None
-        save_case(name, op, inputs, attrs, refs[0], deq, {"test": fn, "kwargs": kw})
+        # test_mamba checks y, then the ssm state, then the conv state (tests/test_bolt_ops.py:304-305)
+        extra = {"ssm": refs[1], "conv": refs[2]} if op == "MambaStep" else None
+        save_case(name, op, inputs, attrs, refs[0], deq, {"test": fn, "kwargs": kw}, extra)
         print(f"{name:28s} {op:10s} ref{tuple(refs[0].shape)}")
 
 

@@ -33,6 +33,8 @@ class Case:
             self.inputs.append(t)
         self.ref = torch.from_numpy(z["ref"].copy())
         self.gguf_deq = torch.from_numpy(z["gguf_deq"].copy()) if "gguf_deq" in z.files else None
+        # further expected tensors of a case (e.g. MambaStep's ssm and conv states)
+        self.extra = {k[4:]: torch.from_numpy(z[k].copy()) for k in z.files if k.startswith("ref_")}
 
     def __repr__(self):
         return f"Case({self.name})"

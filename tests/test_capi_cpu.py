@@ -128,3 +128,33 @@ def test_relu2_validation_and_empty():
     assert "Relu2: negative dimension" in _lib.last_error()
     xs, k2 = _sh(0, 1000)  # nothing to do: no device work, no pointer needed
     assert lib.bolt_relu2(NULL, xs, 2, NULL, NULL) == 0
+
+
+def _call_mamba(proj_shape, cs_shape, ss_shape, hd=64, ds=128, heads=16, ng=4, sel=False):
+    lib = _lib.lib()
+    ps, k1 = _sh(*proj_shape)
+    cs, k2 = _sh(*cs_shape)
+    ss, k3 = _sh(*ss_shape)
+    head = [NULL, ps, len(proj_shape), NULL, cs, len(cs_shape), NULL, ss, len(ss_shape)] + [NULL] * 6
+    tail = [heads, hd, ds, ng, 1e-5, 1e-3] + [NULL] * 6
+    if sel:
+        rc = lib.bolt_mamba_verify(*head, ctypes.c_void_p(16), *tail)
+    else:
+        rc = lib.bolt_mamba_step(*head, *tail)
+    return rc, _lib.last_error()
+
+
+@pytest.mark.parametrize("kw,msg", [
+    (dict(hd=32), "MambaStep: only head_dim=64, d_state=128 are implemented"),
+    (dict(proj_shape=(17, 3088)), "MambaStep: rows must be in [1,16]"),
+    (dict(proj_shape=(2, 3000)), "MambaStep: bad proj width"),
+    (dict(ng=3), "MambaStep: heads must be a multiple of n_groups"),
+    (dict(proj_shape=(4, 3088), sel=True), "MambaVerify: state buffer needs >= R rows"),
+    (dict(cs_shape=(2, 2048, 4)), "MambaStep: conv state must be [rows, conv_dim, 3]"),
+    (dict(ss_shape=(2, 16, 128, 32)), "MambaStep: ssm state must be"),
+])
+def test_mamba_validation(kw, msg):
+    args = dict(proj_shape=(2, 3088), cs_shape=(2, 2048, 3), ss_shape=(2, 16, 128, 64))
+    args.update(kw)
+    rc, err = _call_mamba(**args)
+    assert rc != 0 and msg in err, err

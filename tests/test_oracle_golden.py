@@ -145,3 +145,15 @@ def test_relu2_oracle():
     s = torch.tensor([float("nan"), -0.0, 0.0, -1e30, 1e30, float("inf"), -float("inf"), 1e-30, 2.5],
                      dtype=torch.bfloat16)
     assert O.relu2(s).float().tolist()[:8] == [0.0, 0.0, 0.0, 0.0, float("inf"), float("inf"), 0.0, 0.0]
+
+
+@pytest.mark.parametrize("name", case_names("mamba_"))
+def test_mamba_oracle(name):
+    c = load(name)
+    a = c.attrs
+    y, cst, sst, _xbc, _ypre = O.mamba_step(*c.inputs, a["heads"], a["head_dim"], a["d_state"], a["n_groups"],
+                                            a["epsilon"], a["time_step_min"])
+    # the reference test's thresholds (tests/test_bolt_ops.py:305), met here to rounding noise
+    assert rel(y, c.ref) < 1e-6
+    assert rel(sst[-1], c.extra["ssm"]) < 1e-6
+    assert rel(cst[-1].float(), c.extra["conv"]) < 1e-6
