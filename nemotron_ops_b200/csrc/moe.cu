@@ -419,18 +419,33 @@ __global__ void __launch_bounds__(256) moe_finalize_kernel(float* __restrict__ p
   const int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
   if (i >= static_cast<int64_t>(R) * Nout) return;
   const int t = static_cast<int>(i / Nout), n = static_cast<int>(i % Nout);
+  // batches of 8 pairs: their ids, then their values, load together (two round trips per batch
+  // instead of two per pair); the sum stays in k order
+  constexpr int kB = 8;
   float a = 0.f;
-  for (int k = 0; k < topk; ++k) {
-    const int pp = t * topk + k;
-    const int e = idx[pp];
-    if (e >= e_begin && e < e_end) {
-      const int64_t o = static_cast<int64_t>(pp) * Nout + n;
-      float v = part[o];
+  for (int k0 = 0; k0 < topk; k0 += kB) {
+    bool use[kB];
+    float v[kB], wk[kB];
+#pragma unroll
+    for (int j = 0; j < kB; ++j) {
+      const int k = k0 + j;
+      const int e = k < topk ? idx[t * topk + k] : -1;
+      use[j] = k < topk && e >= e_begin && e < e_end;
+    }
+#pragma unroll
+    for (int j = 0; j < kB; ++j) {
+      const int pp = t * topk + k0 + j;
+      v[j] = use[j] ? part[static_cast<int64_t>(pp) * Nout + n] : 0.f;
+      wk[j] = use[j] ? w[pp] : 0.f;
+    }
+#pragma unroll
+    for (int j = 0; j < kB; ++j) {
+      if (!use[j]) continue;
       if (round_part) {
-        v = __bfloat162float(__float2bfloat16(v));
-        part[o] = v;
+        v[j] = __bfloat162float(__float2bfloat16(v[j]));
+        part[static_cast<int64_t>(t * topk + k0 + j) * Nout + n] = v[j];
       }
-      a = fmaf(w[pp], v, a);
+      a = fmaf(wk[j], v[j], a);
     }
   }
   if (out) out[i] = __float2bfloat16(a);
