@@ -726,33 +726,45 @@ cudaError_t launch_moe_group(const int* idx, int P, int topk, int e_begin, int e
 // round_part: part holds fp32 fc2 sums, rounded to bf16 (and written back) here
 cudaError_t launch_moe_finalize(float* part, int round_part, const float* w, const int* idx, int R, int topk,
                                 int e_begin, int e_end, bf16* out, float* out_partial, const LaunchCfg& cfg);
-// tcgen05 expert layer (moe_umma.cu); cudaErrorNotSupported when the shape or format does not fit.
-// fc1 zeroes part_out when given one; fc2 with split relies on that to split tiles.
-cudaError_t launch_moe_layer_umma(int fmt, int fc, const bf16* x, const int* list, const uint8_t* w, const void* sc,
-                                  bf16* h_out, float* part_out, int P, int R, int E, int e_end, int K, int rows_pg,
-                                  const LaunchCfg& cfg, int split);
+// tcgen05 expert layer (moe_umma.cu): whether it takes a layer, and the launch.  Its CTAs build the
+// expert list from idx themselves; fc1 zeroes part_out when given one (fc2 with split relies on
+// that to split tiles) and writes meta when given meta_out.
+bool moe_layer_umma_ok(int fmt, const void* sc, int P, int K, int rows_pg);
+cudaError_t launch_moe_layer_umma(int fmt, int fc, const bf16* x, const int* idx, int topk, int e_begin, int* meta_out,
+                                  const uint8_t* w, const void* sc, bf16* h_out, float* part_out, int P, int R, int E,
+                                  int e_end, int K, int rows_pg, const LaunchCfg& cfg, int split);
 
 cudaError_t launch_moe_verify(int fmt, const bf16* z, const int* idx, const float* w, const uint8_t* fc1_w,
                               const bf16* fc1_s, const uint8_t* fc2_w, const bf16* fc2_s, int R, int E, int I,
                               int topk, int e_begin, int e_end, bf16* out, bf16* h, float* part, int* meta,
                               float* out_partial, const LaunchCfg& cfg) {
   const int P = R * topk;
-  cudaError_t e = launch_moe_group(idx, P, topk, e_begin, e_end, meta, cfg);
-  if (e != cudaSuccess) return e;
+  // tcgen05 layers where they apply (int4 / native IQ2_XXS, 128-row tiles), else mma.sync.  The
+  // tcgen05 layers build the expert list from idx in every CTA; the grouping kernel (which writes
+  // meta, read by the mma.sync layers) runs only when a layer falls back, else fc1 writes meta.
+  const bool u1 = moe_layer_umma_ok(fmt, fc1_s, P, 1024, I), u2 = moe_layer_umma_ok(fmt, fc2_s, P, I, 1024);
+  const bool group = !(u1 && u2);
   LaunchCfg c2 = cfg;
   c2.pdl = true;  // same op: each kernel waits for its predecessor with griddepcontrol.wait
-  // tcgen05 layers where they apply (int4 / native IQ2_XXS, 128-row tiles), else mma.sync
+  cudaError_t e = cudaSuccess;
+  if (group) {
+    e = launch_moe_group(idx, P, topk, e_begin, e_end, meta, cfg);
+    if (e != cudaSuccess) return e;
+  }
   // the tcgen05 fc1 also zeroes part (16-byte aligned), which lets the tcgen05 fc2 split tiles
   const bool part16 = (reinterpret_cast<uintptr_t>(part) & 15) == 0;
-  e = launch_moe_layer_umma(fmt, 1, z, meta, fc1_w, fc1_s, h, part16 ? part : nullptr, P, R, E, e_end, 1024, I, c2,
-                            0);
-  const bool zeroed = e == cudaSuccess && part16;
-  if (e == cudaErrorNotSupported)
+  if (u1)
+    e = launch_moe_layer_umma(fmt, 1, z, idx, topk, e_begin, group ? nullptr : meta, fc1_w, fc1_s, h,
+                              part16 ? part : nullptr, P, R, E, e_end, 1024, I, group ? c2 : cfg, 0);
+  else
     e = launch_grouped(fmt, false, 1, true, z, meta, idx, fc1_w, fc1_s, h, nullptr, P, R, topk, E, e_begin, e_end,
                        1024, I, c2);
   if (e != cudaSuccess) return e;
-  e = launch_moe_layer_umma(fmt, 2, h, meta, fc2_w, fc2_s, nullptr, part, P, R, E, e_end, I, 1024, c2, zeroed ? 1 : 0);
-  if (e == cudaErrorNotSupported)
+  const bool zeroed = u1 && part16;
+  if (u2)
+    e = launch_moe_layer_umma(fmt, 2, h, idx, topk, e_begin, nullptr, fc2_w, fc2_s, nullptr, part, P, R, E, e_end, I,
+                              1024, c2, zeroed ? 1 : 0);
+  else
     e = launch_grouped(fmt, false, 2, true, h, meta, idx, fc2_w, fc2_s, nullptr, part, P, R, topk, E, e_begin, e_end,
                        I, 1024, c2);
   if (e != cudaSuccess) return e;

@@ -58,7 +58,9 @@ constexpr uint32_t kIdesc = (1u << 4) | (1u << 7) | (1u << 10) | ((16u >> 3) << 
 
 struct UmmaParams {
   const bf16* x;        // fc1: z [R, K]; fc2: h [P, K]
-  const int* list;      // meta: [0] = U, experts, then 8 pairs per expert
+  const int* idx;       // expert id of each (token, k) pair [P]; pair p is token p / topk
+  int topk, e_begin;    // pairs whose expert is outside [e_begin, e_end) are not computed
+  int* meta_out;        // fc1: CTA 0 writes the op's meta output here (null: written elsewhere)
   const uint8_t* w;     // expert rows [E * rows_pg, row_bytes]
   const uint8_t* sc;    // [E * rows_pg, sc_row_bytes]
   bf16* h_out;          // fc1 output [P, rows_pg]
@@ -81,14 +83,62 @@ __device__ __forceinline__ int ldcg_i(const int* p) {
   asm volatile("ld.global.cg.s32 %0, [%1];" : "=r"(v) : "l"(p));
   return v;
 }
-__device__ __forceinline__ int group_expert(const UmmaParams& p, int g) { return ldcg_i(p.list + 1 + g); }
-__device__ __forceinline__ int column_pair(const UmmaParams& p, int g, int j) {
-  return ldcg_i(p.list + 1 + p.P + 8 * g + j);
+// The call's groups -- one per selected expert, in first-occurrence order over the pairs, each
+// with the pair of every token row (or -1) -- built by every CTA in shared memory from idx (the
+// layout of the op's meta output: src/bolt_ops.cu:1084-1112).
+constexpr int kMaxPairs = 128;
+struct GroupList {
+  int n;                              // groups (unique local experts)
+  int exp[kMaxPairs];                 // expert of group g
+  signed char pair[kMaxPairs * 8];    // pair of (group g, token row j), -1 for none
+  int idx[kMaxPairs];                 // (build scratch) the pairs' expert ids
+  int rank[kMaxPairs];                // (build scratch) group of a first-occurrence pair
+  int wtot[kMaxPairs / 32];           // (build scratch) first occurrences per warp
+};
+
+// All threads of the CTA; ends with a CTA barrier.  idx is read at L2 (fc2 reads it before its
+// dependency wait: fc1 triggers fc2 only after its own wait, so idx is final by then).
+__device__ void build_group_list(const UmmaParams& p, GroupList& gl) {
+  const int t = threadIdx.x, lane = t & 31, warp = t >> 5;
+  for (int i = t; i < 8 * p.P; i += blockDim.x) gl.pair[i] = -1;
+  const int e = t < p.P ? __ldcg(p.idx + t) : -1;
+  if (t < p.P) gl.idx[t] = e;
+  __syncthreads();
+  const bool local = t < p.P && e >= p.e_begin && e < p.e_end;
+  int first = -1;
+  if (local)
+    for (int j = 0; j <= t; ++j)
+      if (gl.idx[j] == e) {
+        first = j;
+        break;
+      }
+  const bool lead = local && first == t;
+  const unsigned bal = __ballot_sync(0xffffffffu, lead);
+  if (warp < kMaxPairs / 32 && lane == 0) gl.wtot[warp] = __popc(bal);
+  __syncthreads();
+  if (lead) {
+    int off = 0;
+    for (int w = 0; w < warp; ++w) off += gl.wtot[w];
+    const int g = off + __popc(bal & ((1u << lane) - 1u));
+    gl.rank[t] = g;
+    gl.exp[g] = e;
+  }
+  if (t == 0) {
+    int u = 0;
+    for (int w = 0; w < kMaxPairs / 32; ++w) u += gl.wtot[w];
+    gl.n = u;
+  }
+  __syncthreads();
+  if (local) gl.pair[gl.rank[first] * 8 + t / p.topk] = static_cast<signed char>(t);
+  __syncthreads();
 }
+
+__device__ __forceinline__ int group_expert(const GroupList& gl, int g) { return gl.exp[g]; }
+__device__ __forceinline__ int column_pair(const GroupList& gl, int g, int j) { return gl.pair[8 * g + j]; }
 template <int FC>
-__device__ __forceinline__ int column_xrow(const UmmaParams& p, int g, int j) {
+__device__ __forceinline__ int column_xrow(const UmmaParams& p, const GroupList& gl, int g, int j) {
   if (FC == 1) return j < p.R ? j : -1;
-  return column_pair(p, g, j);
+  return column_pair(gl, g, j);
 }
 
 __device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
@@ -191,14 +241,15 @@ __device__ __forceinline__ uint4 x_piece_order(uint4 v) {
 }
 
 template <int FC>
-__device__ __forceinline__ void issue_x(const UmmaParams& p, uint8_t* xs, uint64_t* x_bar, int g, int buf) {
+__device__ __forceinline__ void issue_x(const UmmaParams& p, const GroupList& gl, uint8_t* xs, uint64_t* x_bar, int g,
+                                        int buf) {
   uint32_t tx = 0;
   for (int j = 0; j < 8; ++j)
-    if (column_xrow<FC>(p, g, j) >= 0) tx += static_cast<uint32_t>(p.K) * 2u;
+    if (column_xrow<FC>(p, gl, g, j) >= 0) tx += static_cast<uint32_t>(p.K) * 2u;
   const uint32_t xb = smem_u32(&x_bar[buf]);
   mbar_arrive_expect_tx(xb, tx);
   for (int j = 0; j < 8; ++j) {
-    const int xr = column_xrow<FC>(p, g, j);
+    const int xr = column_xrow<FC>(p, gl, g, j);
     if (xr >= 0)
       bulk_g2s(smem_u32(xs + static_cast<size_t>(buf) * p.xs_bytes + static_cast<size_t>(j) * p.K * 2),
                p.x + static_cast<int64_t>(xr) * p.K, static_cast<uint32_t>(p.K) * 2u, xb);
@@ -230,6 +281,7 @@ __global__ void __launch_bounds__(kUThreads, 1)
   __shared__ uint64_t af_bar[kASlots], ae_bar[kASlots], df_bar[2], de_bar[2], done_bar;
   __shared__ __align__(16) uint32_t grid_s[(FMT == kFmtIq2N) ? 1024 : 4];
   __shared__ int cols_s[3][8];
+  __shared__ GroupList gl;
   __shared__ uint32_t tmem_base;
   __shared__ volatile int abort_flag;
   uint8_t* smem = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
@@ -275,26 +327,39 @@ __global__ void __launch_bounds__(kUThreads, 1)
   tc_fence_after();
   const uint32_t tb = tmem_base;
   if constexpr (FC == 1) {
-    pdl_wait();  // meta is the previous kernel's output
+    pdl_wait();  // idx is the previous kernel's output
     pdl_trigger();
+  } else {
+    pdl_trigger();
+  }
+  build_group_list(p, gl);
+  const int ngroups = gl.n;
+  if constexpr (FC == 1) {
     // fc2's output rows of the listed pairs start at zero (this CTA's share of the 8 slots per
     // group; other rows stay untouched; fc2 adds into them only after this grid completes)
     if (p.part_out != nullptr) {
-      const int nslots = 8 * ldcg_i(p.list);
+      const int nslots = 8 * ngroups;
       const int c4 = p.zero_cols >> 2;
       for (int j = static_cast<int>(static_cast<int64_t>(blockIdx.x) * nslots / gridDim.x),
                j1 = static_cast<int>(static_cast<int64_t>(blockIdx.x + 1) * nslots / gridDim.x);
            j < j1; ++j) {
-        const int pp = ldcg_i(p.list + 1 + p.P + j);
+        const int pp = gl.pair[j];
         if (pp < 0) continue;
         float4* row = reinterpret_cast<float4*>(p.part_out + static_cast<int64_t>(pp) * p.zero_cols);
         for (int i = tid; i < c4; i += kUThreads) row[i] = make_float4(0.f, 0.f, 0.f, 0.f);
       }
     }
-  } else {
-    pdl_trigger();
+    // the op's meta output: [0] = groups, [1 + g] = expert (-1 past the groups), then the pairs
+    if (p.meta_out != nullptr && blockIdx.x == 0) {
+      for (int i = tid; i < 1 + 9 * p.P; i += kUThreads) {
+        int v;
+        if (i == 0) v = ngroups;
+        else if (i <= p.P) v = i - 1 < ngroups ? gl.exp[i - 1] : -1;
+        else v = gl.pair[i - 1 - p.P];
+        p.meta_out[i] = v;
+      }
+    }
   }
-  const int ngroups = ldcg_i(p.list);
   const int64_t T = static_cast<int64_t>(ngroups) * tpg;
   // This CTA's work: tiles [t0, t0 + ntl), K segments [seg_lo(ti), seg_hi(ti)) of tile ti.  fc2
   // divides the flat list of (tile, K segment) stages evenly when there are at least as many tiles
@@ -329,7 +394,7 @@ __global__ void __launch_bounds__(kUThreads, 1)
       const int first = min(min(NS, nstages), p.nsbuf * KS - q_first);
       // stage cursor: slot s (use `round`), K segment q of tile ti (tile tig of group g), scale buffer sb
       int s = 0, round = 0, q = q_first, ti = 0, tig = t0 - g0 * tpg, g = g0, sb = 0;
-      int cur_e = group_expert(p, g0);
+      int cur_e = group_expert(gl, g0);
       int prow = cur_e * p.rows_pg + tig * kTileRows;
       auto advance = [&]() {
         if (++s == NS) s = 0, ++round;
@@ -340,7 +405,7 @@ __global__ void __launch_bounds__(kUThreads, 1)
           if (++tig == tpg) {
             tig = 0;
             ++g;
-            if (ti < ntl) cur_e = group_expert(p, g);
+            if (ti < ntl) cur_e = group_expert(gl, g);
           }
           prow = cur_e * p.rows_pg + tig * kTileRows;
         }
@@ -351,7 +416,7 @@ __global__ void __launch_bounds__(kUThreads, 1)
         advance();
       }
       pdl_wait();  // activations (z, or h of fc1) are ready
-      issue_x<FC>(p, xs, x_bar, g0, 0);
+      issue_x<FC>(p, gl, xs, x_bar, g0, 0);
       int xk = 0;  // ordinal of the last group whose activations were issued
       bool okw = true;
       int issued = first;
@@ -363,7 +428,7 @@ __global__ void __launch_bounds__(kUThreads, 1)
           if (kn >= p.nxb && !abort_flag)
             okw = mbar_wait(smem_u32(&xf_bar[kn % p.nxb]), ((kn / p.nxb) - 1) & 1, kStatusEmptyWait);
           if (okw && !abort_flag) {
-            issue_x<FC>(p, xs, x_bar, g0 + kn, kn % p.nxb);
+            issue_x<FC>(p, gl, xs, x_bar, g0 + kn, kn % p.nxb);
             xk = kn;
           }
           if (abort_flag) okw = false;
@@ -518,10 +583,10 @@ __global__ void __launch_bounds__(kUThreads, 1)
           __syncwarp();
           if (lane == 0) mbar_arrive(smem_u32(&xr_bar[xb]));
         }
-        if (tid < 8) cols_s[kg % 3][tid] = column_pair(p, gg, tid);
+        if (tid < 8) cols_s[kg % 3][tid] = column_pair(gl, gg, tid);
         if constexpr (FMT == kFmtIq2N)
           sc_mis = static_cast<uint32_t>(
-              reinterpret_cast<uintptr_t>(p.sc + static_cast<int64_t>(group_expert(p, gg)) * p.rows_pg * sc_rb) & 15);
+              reinterpret_cast<uintptr_t>(p.sc + static_cast<int64_t>(group_expert(gl, gg)) * p.rows_pg * sc_rb) & 15);
         named_bar_sync(1, kDecW * 32);
       }
       const uint8_t* sct = smem + p.sc_off + static_cast<size_t>(sbuf) * p.sc_bytes + sc_mis;
@@ -633,22 +698,42 @@ cudaError_t launch_umma(const CUtensorMap& tmw, const UmmaParams& p, size_t smem
   return launch_kernel(kern, dim3(cfg.sms), dim3(kUThreads), smem, cfg, tmw, p);
 }
 
+// Static shared memory of a kernel instance (the dynamic carve-out gets the rest of the 227 KB).
+template <int FMT, int FC>
+size_t umma_static_smem() {
+  static const size_t bytes = [] {
+    cudaFuncAttributes a{};
+    return cudaFuncGetAttributes(&a, moe_umma_kernel<FMT, FC>) == cudaSuccess ? a.sharedSizeBytes : size_t(16384);
+  }();
+  return bytes;
+}
+
 }  // namespace
 
-// One MoeVerify expert layer (fc1: K = 1024, rows_pg = I; fc2: K = I, rows_pg = 1024) on the
-// tcgen05 path.  fc1 with part_out set zeroes the listed pairs' rows of part_out [P, 1024] (fc2's
-// output); fc2 with split (those rows zeroed) divides its stages evenly, splitting tiles between
-// CTAs.  cudaErrorNotSupported when the shapes or the format do not fit (the caller then uses the
-// mma.sync kernel of moe_tc.cu).
-cudaError_t launch_moe_layer_umma(int fmt, int fc, const bf16* x, const int* list, const uint8_t* w, const void* sc,
-                                  bf16* h_out, float* part_out, int P, int R, int E, int e_end, int K, int rows_pg,
-                                  const LaunchCfg& cfg, int split) {
-  if (fmt != kFmtQ4 && fmt != kFmtIq2N) return cudaErrorNotSupported;
+bool moe_layer_umma_ok(int fmt, const void* sc, int P, int K, int rows_pg) {
+  if (fmt != kFmtQ4 && fmt != kFmtIq2N) return false;
   // the activation rows (8 x K / 8 pieces of 16 bytes) are permuted through registers
-  if (rows_pg % kTileRows || K % kKStep || K > kMaxXPieces * kDecW * 32 || P > 128) return cudaErrorNotSupported;
+  if (rows_pg % kTileRows || K % kKStep || K > kMaxXPieces * kDecW * 32 || P > kMaxPairs || P < 1) return false;
+  // int4 scales are read as 8-byte words: the span of every tile must start 16-byte aligned
+  const int64_t srb = fmt_scale_row_bytes(fmt, K);
+  return !(fmt == kFmtQ4 && (srb % 16 || (reinterpret_cast<uintptr_t>(sc) & 15)));
+}
+
+// One MoeVerify expert layer (fc1: K = 1024, rows_pg = I; fc2: K = I, rows_pg = 1024) on the
+// tcgen05 path, over the pairs of idx whose expert is in [e_begin, e_end).  fc1 with part_out set
+// zeroes the listed pairs' rows of part_out [P, 1024] (fc2's output), and with meta_out set
+// writes the op's meta output; fc2 with split (those rows zeroed) divides its stages evenly,
+// splitting tiles between CTAs.  cudaErrorNotSupported when moe_layer_umma_ok says no.
+cudaError_t launch_moe_layer_umma(int fmt, int fc, const bf16* x, const int* idx, int topk, int e_begin, int* meta_out,
+                                  const uint8_t* w, const void* sc, bf16* h_out, float* part_out, int P, int R, int E,
+                                  int e_end, int K, int rows_pg, const LaunchCfg& cfg, int split) {
+  if (!moe_layer_umma_ok(fmt, sc, P, K, rows_pg)) return cudaErrorNotSupported;
   UmmaParams p{};
   p.x = x;
-  p.list = list;
+  p.idx = idx;
+  p.topk = topk;
+  p.e_begin = e_begin;
+  p.meta_out = fc == 1 ? meta_out : nullptr;
   p.w = w;
   p.sc = static_cast<const uint8_t*>(sc);
   p.h_out = h_out;
@@ -669,8 +754,6 @@ cudaError_t launch_moe_layer_umma(int fmt, int fc, const bf16* x, const int* lis
   p.pb = fmt == kFmtQ4 ? 128 : 64;  // one 256-element K step per piece
   const int pieces = static_cast<int>(rb / p.pb);
   p.sc_rb = static_cast<int>(srb);
-  // int4 scales are read as 8-byte words: the span of every tile must start 16-byte aligned
-  if (fmt == kFmtQ4 && (srb % 16 || (reinterpret_cast<uintptr_t>(sc) & 15))) return cudaErrorNotSupported;
   // pieces per stage: the largest divisor of the row's pieces with a stage of <= 48 KB (each
   // tensor copy costs a fixed ~0.2-0.7 us to issue, more while the decode warps keep the SM busy)
   p.sp = 1;
@@ -681,7 +764,10 @@ cudaError_t launch_moe_layer_umma(int fmt, int fc, const bf16* x, const int* lis
   p.w_stride = (p.w_bytes + 1023u) & ~1023u;
   p.sc_bytes = static_cast<uint32_t>((srb * kTileRows + 32 + 127) & ~int64_t(127));
   p.xs_bytes = (static_cast<uint32_t>(8 * K * 2) + 1023u) & ~1023u;
-  const size_t budget = cfg.smem_budget ? cfg.smem_budget : 220 * 1024;
+  const size_t static_smem = fmt == kFmtQ4 ? (fc == 1 ? umma_static_smem<kFmtQ4, 1>() : umma_static_smem<kFmtQ4, 2>())
+                                           : (fc == 1 ? umma_static_smem<kFmtIq2N, 1>() : umma_static_smem<kFmtIq2N, 2>());
+  const size_t smem_cap = 227 * 1024 - static_smem;  // dynamic bytes a CTA may have
+  const size_t budget = std::min(cfg.smem_budget ? cfg.smem_budget : 220 * 1024, smem_cap - 1024);
   auto nsbuf_for = [](int ns, int kseg) { return std::min(4, (ns + kseg - 1) / kseg + 1); };
   // one or two activation buffers: whichever leaves more weight bytes in flight (ties: two, so
   // the next group's rows land while this group computes)
@@ -705,7 +791,7 @@ cudaError_t launch_moe_layer_umma(int fmt, int fc, const bf16* x, const int* lis
   p.xs_off = (p.xs_off + 1023u) & ~1023u;
   // at least 116 KB, so that one CTA holds the SM (the kernel allocates all 512 TMEM columns)
   const size_t smem = std::max<size_t>(1024 + p.xs_off + static_cast<size_t>(p.nxb) * p.xs_bytes, 116 * 1024);
-  if (smem > 227 * 1024) return cudaErrorNotSupported;
+  if (smem > smem_cap) return cudaErrorNotSupported;
   CUtensorMap tmw;
   if (!row_tile_map(&tmw, w, static_cast<int64_t>(E) * rows_pg, rb, p.sp, p.pb, kTileRows)) return cudaErrorNotSupported;
   if (fmt == kFmtQ4) return fc == 1 ? launch_umma<kFmtQ4, 1>(tmw, p, smem, cfg) : launch_umma<kFmtQ4, 2>(tmw, p, smem, cfg);
