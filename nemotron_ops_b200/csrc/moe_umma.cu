@@ -7,8 +7,9 @@
 // D[128 rows, 16 cols] = A[128 rows, K] * B[16 cols, K]^T with
 //   * A: the expert's weight rows, decoded to bf16 by 16 decode warps straight into tensor
 //     memory (tcgen05.st): thread (warp w, lane l) owns row 32 * (w & 3) + l -- the tensor
-//     memory lane it may address -- and quarter (w >> 2) of each 256-element K step; its 16-byte
-//     shared-memory reads of a 128- or 64-byte-swizzled stage are bank-conflict-free;
+//     memory lane it may address; warps 0-7 decode the even 256-element K steps and warps 8-15
+//     the odd ones, each warp half of a step; its 16-byte shared-memory reads of a 128- or
+//     64-byte-swizzled stage are bank-conflict-free;
 //   * B: the group's 8 activation rows (fc1: z; fc2: the h rows of the expert's pairs) in
 //     shared memory, K-major core matrices (8 rows x 16 bytes) without swizzle; the descriptor's
 //     8-row-group stride is 0, so columns 8..15 repeat columns 0..7 (N = 16 is the smallest
@@ -40,7 +41,13 @@ namespace bolt {
 namespace {
 
 constexpr int kDecW = 16;                   // decode warps: 4 per tensor-memory lane quarter
-constexpr int kParts = kDecW / 4;           // K parts of a K step (one per warp of a quarter)
+constexpr int kParts = kDecW / 4;           // accumulator columns are drained in kParts parts
+// The decode warps form two groups of 8 that take alternate K steps (each warp decodes half a
+// step for its 32 rows), so one group's waits (stage, A slot, tensor-memory stores) overlap the
+// other group's arithmetic instead of idling the SM.
+constexpr int kGroups = 2;
+constexpr int kGroupW = kDecW / kGroups;    // warps per group: 2 per lane quarter
+constexpr int kDParts = kGroupW / 4;        // K parts of a K step within a group
 constexpr int kProdW = kDecW;               // TMA producer warp
 constexpr int kMmaW = kDecW + 1;            // MMA-issuing warp (also owns the tensor memory)
 constexpr int kUThreads = (kDecW + 2) * 32;
@@ -307,7 +314,7 @@ __global__ void __launch_bounds__(kUThreads, 1)
       mbar_init(smem_u32(&de_bar[b]), kDecW);
     }
     for (int a = 0; a < kASlots; ++a) {
-      mbar_init(smem_u32(&af_bar[a]), kDecW);
+      mbar_init(smem_u32(&af_bar[a]), kGroupW);
       mbar_init(smem_u32(&ae_bar[a]), 1);
     }
     mbar_init(smem_u32(&done_bar), 1);
@@ -497,7 +504,8 @@ __global__ void __launch_bounds__(kUThreads, 1)
     }
   } else {
     // ------------------------------------------------------------------ decode warps
-    const int q4 = warp & 3, hh = warp >> 2;  // lane quarter, K part
+    const int q4 = warp & 3, hh = warp >> 2;  // lane quarter, accumulator part
+    const int grp = warp / kGroupW, hd = (warp >> 2) % kDParts;  // K-step group, K part within a step
     const int r = 32 * q4 + lane;             // tile row = tensor memory lane
     const uint32_t lane_off = static_cast<uint32_t>(32 * q4) << 16;
     const int sc_rb = static_cast<int>(fmt_scale_row_bytes(FMT, p.K));
@@ -601,17 +609,18 @@ __global__ void __launch_bounds__(kUThreads, 1)
         for (int kk = 0; kk < p.sp; ++kk) {
           const int ks = q * p.sp + kk;
           const int a = ka % kASlots;
+          const bool mine = ka % kGroups == grp;  // this warp's group decodes K step ks
           // this thread's share of K step ks (weights, scales) goes to registers first; after the
           // stage's last step the slot returns to the producer, so decoding does not hold it
-          constexpr int kU = FMT == kFmtQ4 ? 8 / kParts : 4 / kParts;  // 16-byte units
+          constexpr int kU = FMT == kFmtQ4 ? 8 / kDParts : 4 / kDParts;  // 16-byte units
           uint4 wv[kU];
           uint32_t s4[kU];
           float d = 0.f;
-          if (ok) {
+          if (ok && mine) {
             if constexpr (FMT == kFmtQ4) {  // unit = 32 elements, one bf16 scale block each
               const uint8_t* wp = wst + static_cast<size_t>(kk) * kTileRows * 128 + r * 128;
               // (the host keeps int4 scale spans 16-byte aligned)
-              const uint8_t* spt = sct + r * sc_rb + ks * 16 + hh * (2 * kU);
+              const uint8_t* spt = sct + r * sc_rb + ks * 16 + hd * (2 * kU);
               if constexpr (kU == 4) {
                 const uint2 sv = *reinterpret_cast<const uint2*>(spt);
                 s4[0] = sv.x & 0xFFFFu, s4[1] = sv.x >> 16, s4[2] = sv.y & 0xFFFFu, s4[3] = sv.y >> 16;
@@ -620,17 +629,21 @@ __global__ void __launch_bounds__(kUThreads, 1)
                 s4[0] = sv & 0xFFFFu, s4[1] = sv >> 16;
               }
 #pragma unroll
-              for (int i = 0; i < kU; ++i) wv[i] = lds128(wp + (((kU * hh + i) ^ (r & 7)) << 4));
+              for (int i = 0; i < kU; ++i) wv[i] = lds128(wp + (((kU * hd + i) ^ (r & 7)) << 4));
             } else {  // unit = two 32-element records
               const uint8_t* wp = wst + static_cast<size_t>(kk) * kTileRows * 64 + r * 64;
               d = __half2float(__ushort_as_half(*reinterpret_cast<const uint16_t*>(sct + r * sc_rb + ks * 2)));
 #pragma unroll
-              for (int i = 0; i < kU; ++i) wv[i] = lds128(wp + (((kU * hh + i) ^ ((r >> 1) & 3)) << 4));
+              for (int i = 0; i < kU; ++i) wv[i] = lds128(wp + (((kU * hd + i) ^ ((r >> 1) & 3)) << 4));
             }
           }
           if (kk == p.sp - 1) {  // the arrive releases (orders) the loads above
             __syncwarp();
             if (lane == 0) mbar_arrive(smem_u32(&empty_bar[s]));
+          }
+          if (!mine) {
+            ++ka;
+            continue;
           }
           if (ok && abort_flag) ok = false;
           if (ok && ka >= kASlots && !mbar_wait(smem_u32(&ae_bar[a]), ((ka / kASlots) - 1) & 1, kStatusFullWait)) {
@@ -639,9 +652,9 @@ __global__ void __launch_bounds__(kUThreads, 1)
           }
           ok = __all_sync(0xffffffffu, ok);
           if (ok) {
-            // this thread's part: K elements [hh, hh + 1) * 256 / kParts of the step = columns
-            // [hh, hh + 1) * 128 / kParts of the A slot
-            const uint32_t tcol = tb + lane_off + a_col(a) + (128u / kParts) * hh;
+            // this thread's part: K elements [hd, hd + 1) * 256 / kDParts of the step = columns
+            // [hd, hd + 1) * 128 / kDParts of the A slot
+            const uint32_t tcol = tb + lane_off + a_col(a) + (128u / kDParts) * hd;
             if constexpr (FMT == kFmtQ4) {
 #pragma unroll
               for (int i = 0; i < kU; ++i) {
