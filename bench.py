@@ -542,7 +542,9 @@ def main():
     ap.add_argument("--workload", default="nvfp4_r1", choices=sorted(WORKLOADS))
     ap.add_argument("--no-extra", action="store_true", help="skip the other configs")
     ap.add_argument("--no-cpu", action="store_true", help="skip the cpu_baseline leg")
-    ap.add_argument("--pdl", type=int, default=0, help="launch with programmatic dependent launch (1) or not (0)")
+    ap.add_argument("--pdl", type=int, default=1, choices=[0, 1, 2],
+                    help="0: plain launches; 1: programmatic dependent launch (the library default); "
+                         "2: PDL with early weight streaming")
     args = ap.parse_args()
     args.steps = max(1, args.steps)
     args.warmup = max(3, args.warmup)
@@ -553,8 +555,7 @@ def main():
     world, rank, local = dist_setup()
 
     from nemotron_ops_b200 import ops
-    if args.pdl:
-        ops.set_launch_options(pdl=True, early_weights=True)
+    ops.set_launch_options(pdl=args.pdl >= 1, early_weights=args.pdl == 2)
     device = f"cuda:{local}"
     hbm, peak_kind = peaks()
     desc, builder = WORKLOADS[args.workload]
@@ -626,7 +627,7 @@ def main():
                        "bytes_per_call": wl["bytes"],
                        "cache": f"inputs larger than L2: {copies} distinct weight copies ({copies_bytes / 1e6:.0f} MB) "
                                 f"rotated inside every step", "parallelism": "replicas" if world > 1 else "single",
-                       "pdl": bool(args.pdl)},
+                       "launch": ("plain", "pdl", "pdl+early_weights")[args.pdl]},
             "roofline": {"bound": "hbm", "achieved": round(wl["bytes"] / (m["us_call"] * 1e3), 1), "peak": hbm,
                          "unit": "GB/s", "frac": round(wl["bytes"] / (m["us_call"] * 1e3) / hbm, 4),
                          "traffic": traffic, "peak_source": peak_kind, "kernel": wl["kernel"]},

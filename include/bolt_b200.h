@@ -50,12 +50,15 @@ BOLT_API int bolt_abi_version(void);
 /*
  * Launch options shared by all ops (process-wide; also read once from the environment
  * variables BOLT_PDL, BOLT_EARLY_WEIGHTS and BOLT_SMEM_BUDGET).
- *   pdl            1: launch the first kernel of an op with programmatic dependent launch,
- *                  so it is scheduled while the previous kernel of the stream drains (it
- *                  still waits for that kernel before touching activations or outputs).
+ *   pdl            1 (default): launch the first kernel of an op with programmatic dependent
+ *                  launch, so it is scheduled while the previous kernel of the stream drains
+ *                  (it still waits for that kernel before touching activations, weights or
+ *                  outputs, so results do not change; a preceding kernel that does not trigger
+ *                  its dependents early simply completes first).  0: ordinary launches.
  *   early_weights  1: with pdl, stream weights before that wait.  Only valid when the
  *                  kernel immediately preceding an op on the stream does not write the op's
  *                  weights or scales (true for inference graphs with constant weights).
+ *                  Default 0.
  *   smem_budget    shared-memory bytes per CTA for staged weights (0 = default).
  * No counterpart in the reference (it has debug knobs BOLT_GEMV_CFG / BOLT_MOE_CFG only).
  */

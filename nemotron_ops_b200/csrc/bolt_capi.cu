@@ -26,7 +26,7 @@ namespace {
 thread_local std::string g_last_error;
 
 struct Options {
-  std::atomic<int> pdl{0};
+  std::atomic<int> pdl{1};  // on by default: every kernel still waits before reading upstream data
   std::atomic<int> early{0};
   std::atomic<int64_t> budget{0};
   Options() {
