@@ -169,6 +169,29 @@ BOLT_API int bolt_moe_verify_shard(const void* z, const int64_t* z_shape, int z_
                           int64_t e_end, void* out, void* h, void* part, void* meta, void* out_partial, void* stream);
 
 /*
+ * Expert-sharded MoeVerify step with the cross-GPU sum built in (no counterpart in the
+ * reference, which is single-GPU): bolt_moe_verify_shard, an fp32 all-reduce of the partials and
+ * bolt_f32_to_bf16 in one call, with no NCCL.  The last kernel writes this rank's partial into
+ * its peer-visible buffer, exchanges flags with the other ranks over NVLink peer memory and adds
+ * all ranks' partials in rank order, so `out` bf16 [R, 1024] holds identical bits on every
+ * rank.  Every rank of the group must make the same sequence of calls.
+ *   peer_bufs   device array [world] of float*: every rank's peer-visible buffer of
+ *               2 * half_floats floats (half_floats >= R * 1024) followed by 16 * world uint32
+ *               flag words that are zero before the first call
+ *   counters    this rank's 16 uint32 call counters (device memory, zero before the first call)
+ * Other arguments as bolt_moe_verify_shard (h, part, meta are scratch outputs).  A rank whose
+ * peers do not arrive within 2 s stops waiting, leaves `out` unwritten and sets bit 4 of the
+ * device status word.
+ */
+BOLT_API int bolt_moe_verify_shard_allreduce(const void* z, const int64_t* z_shape, int z_rank, const void* idx,
+                                             const void* w, const void* fc1_w, const int64_t* fc1_w_shape,
+                                             int fc1_w_rank, const void* fc1_s, const void* fc2_w, const void* fc2_s,
+                                             int64_t topk, int64_t iq2, int64_t e_begin, int64_t e_end, void* h,
+                                             void* part, void* meta, const void* peer_bufs, void* counters,
+                                             int64_t half_floats, int64_t rank, int64_t world, void* out,
+                                             void* stream);
+
+/*
  * Expert-sharded MoeDecode step (no counterpart in the reference).  As bolt_moe_verify_shard:
  * only pairs whose expert is in [e_begin, e_end) are computed (h / part rows of the other pairs
  * are left untouched), out_partial f32 [R, 1024] receives their weighted sum for the caller to

@@ -27,6 +27,8 @@ SIGNATURES = {
     "bolt_moe_verify_noalloc": (_I, [_P, _S, _I, _P, _P, _P, _S, _I, _P, _P, _P, _L, _L, _P, _P]),
     "bolt_moe_verify_shard": (_I, [_P, _S, _I, _P, _P, _P, _S, _I, _P, _P, _P, _L, _L, _L, _L, _P, _P, _P, _P, _P,
                                    _P]),
+    "bolt_moe_verify_shard_allreduce": (_I, [_P, _S, _I, _P, _P, _P, _S, _I, _P, _P, _P, _L, _L, _L, _L, _P, _P, _P,
+                                             _P, _P, _L, _L, _L, _P, _P]),
     "bolt_moe_decode_shard": (_I, [_P, _S, _I, _P, _P, _P, _S, _I, _P, _P, _P, _L, _L, _L, _P, _P, _P, _P, _P]),
     "bolt_mamba_step": (_I, [_P, _S, _I, _P, _S, _I, _P, _S, _I, _P, _P, _P, _P, _P, _P, _L, _L, _L, _L, _F, _F,
                              _P, _P, _P, _P, _P, _P]),

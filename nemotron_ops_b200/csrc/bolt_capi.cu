@@ -121,7 +121,8 @@ __global__ void f32_to_bf16_kernel(const float* __restrict__ in, bf16* __restric
 int moe_verify_impl(const void* z, const int64_t* z_shape, int z_rank, const void* idx, const void* w,
                     const void* fc1_w, const int64_t* fc1_w_shape, int fc1_w_rank, const void* fc1_s,
                     const void* fc2_w, const void* fc2_s, int64_t topk, int64_t iq2, int64_t e_begin, int64_t e_end,
-                    bool sharded, void* out, void* h, void* part, void* meta, void* out_partial, void* stream) {
+                    bool sharded, void* out, void* h, void* part, void* meta, void* out_partial, void* stream,
+                    const PeerReduce* pr = nullptr) {
   return guarded([&] {
     const Shape zs{z_shape, z_rank}, w1s{fc1_w_shape, fc1_w_rank};
     const int64_t R = zs.dim(0);
@@ -148,7 +149,7 @@ int moe_verify_impl(const void* z, const int64_t* z_shape, int z_rank, const voi
                                    static_cast<int>(I), static_cast<int>(topk), static_cast<int>(e_begin),
                                    static_cast<int>(e_end), static_cast<bf16*>(out), static_cast<bf16*>(h),
                                    static_cast<float*>(part), static_cast<int*>(meta), static_cast<float*>(out_partial),
-                                   make_cfg(stream)));
+                                   make_cfg(stream), pr));
   });
 }
 
@@ -341,6 +342,30 @@ int bolt_moe_verify_shard(const void* z, const int64_t* z_shape, int z_rank, con
                           int64_t e_end, void* out, void* h, void* part, void* meta, void* out_partial, void* stream) {
   return moe_verify_impl(z, z_shape, z_rank, idx, w, fc1_w, fc1_w_shape, fc1_w_rank, fc1_s, fc2_w, fc2_s, topk, iq2,
                          e_begin, e_end, true, out, h, part, meta, out_partial, stream);
+}
+
+int bolt_moe_verify_shard_allreduce(const void* z, const int64_t* z_shape, int z_rank, const void* idx, const void* w,
+                                    const void* fc1_w, const int64_t* fc1_w_shape, int fc1_w_rank, const void* fc1_s,
+                                    const void* fc2_w, const void* fc2_s, int64_t topk, int64_t iq2, int64_t e_begin,
+                                    int64_t e_end, void* h, void* part, void* meta, const void* peer_bufs,
+                                    void* counters, int64_t half_floats, int64_t rank, int64_t world, void* out,
+                                    void* stream) {
+  PeerReduce pr{};
+  const int rc = guarded([&] {
+    require(world >= 1 && world <= 64 && rank >= 0 && rank < world, "MoeVerify allreduce: rank outside [0, world)");
+    require(peer_bufs != nullptr && counters != nullptr && out != nullptr,
+            "MoeVerify allreduce: null peer buffers, counters or output");
+    require(z_rank >= 1 && z_shape != nullptr && half_floats >= z_shape[0] * 1024,
+            "MoeVerify allreduce: peer buffer halves must hold R * 1024 floats");
+    pr.bufs = static_cast<float* const*>(peer_bufs);
+    pr.epoch = static_cast<uint32_t*>(counters);
+    pr.stride = half_floats;
+    pr.rank = static_cast<int>(rank);
+    pr.world = static_cast<int>(world);
+  });
+  if (rc != BOLT_OK) return rc;
+  return moe_verify_impl(z, z_shape, z_rank, idx, w, fc1_w, fc1_w_shape, fc1_w_rank, fc1_s, fc2_w, fc2_s, topk, iq2,
+                         e_begin, e_end, true, out, h, part, meta, nullptr, stream, &pr);
 }
 
 namespace {

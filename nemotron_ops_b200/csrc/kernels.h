@@ -61,6 +61,18 @@ cudaError_t launch_dequant(int fmt, int exact, const uint8_t* w, const void* sc,
 // y = bf16(max(x, 0)^2) over n bf16 values.
 cudaError_t launch_relu2(const bf16* x, bf16* y, int64_t n, const LaunchCfg& cfg);
 
+// ---- NVLink peer reduction of the expert-sharded MoE --------------------------------------
+// bufs: device array of every rank's peer-visible buffer: 2 * stride fp32 partials, then
+// kPeerReduceCtas * world uint32 flag words (zero at start); epoch: this rank's
+// kPeerReduceCtas uint32 call counters (zero at start).
+constexpr int kPeerReduceCtas = 16;
+struct PeerReduce {
+  float* const* bufs;
+  uint32_t* epoch;
+  int64_t stride;
+  int rank, world;
+};
+
 // ---- Mamba ---------------------------------------------------------------------------
 // One MambaStep (sel == null: state row 0 in and out) or MambaVerify (start from row *sel,
 // the state after token r to row r) over R tokens; see mamba.cu.
@@ -102,6 +114,6 @@ cudaError_t launch_moe_decode_simt(const bf16* z, const int* idx, const float* w
 cudaError_t launch_moe_verify(int fmt, const bf16* z, const int* idx, const float* w, const uint8_t* fc1_w,
                               const bf16* fc1_s, const uint8_t* fc2_w, const bf16* fc2_s, int R, int E, int I,
                               int topk, int e_begin, int e_end, bf16* out, bf16* h, float* part, int* meta,
-                              float* out_partial, const LaunchCfg& cfg);
+                              float* out_partial, const LaunchCfg& cfg, const PeerReduce* pr = nullptr);
 
 }  // namespace bolt

@@ -407,18 +407,11 @@ __global__ void __launch_bounds__(128) moe_group_kernel(const int* __restrict__ 
   if (p == 0) meta[0] = wtot[0] + wtot[1] + wtot[2] + wtot[3];
 }
 
-// out[t] = sum over token t's local pairs of w * part (k ascending).  round_part: part holds fp32
+// sum over token t's local pairs of w * part[., n] (k ascending).  round_part: part holds fp32
 // sums; each pair's fc2 output is bf16(part), written back so part holds the per-pair outputs.
-__global__ void __launch_bounds__(256) moe_finalize_kernel(float* __restrict__ part, int round_part,
-                                                           const float* __restrict__ w,
-                                                           const int* __restrict__ idx, int R, int topk, int Nout,
-                                                           int e_begin, int e_end, bf16* __restrict__ out,
-                                                           float* __restrict__ out_f32) {
-  pdl_wait();
-  pdl_trigger();
-  const int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
-  if (i >= static_cast<int64_t>(R) * Nout) return;
-  const int t = static_cast<int>(i / Nout), n = static_cast<int>(i % Nout);
+__device__ __forceinline__ float local_partial(float* __restrict__ part, int round_part, const float* __restrict__ w,
+                                               const int* __restrict__ idx, int t, int n, int topk, int Nout,
+                                               int e_begin, int e_end) {
   // batches of 8 pairs: their ids, then their values, load together (two round trips per batch
   // instead of two per pair); the sum stays in k order
   constexpr int kB = 8;
@@ -448,8 +441,97 @@ __global__ void __launch_bounds__(256) moe_finalize_kernel(float* __restrict__ p
       a = fmaf(wk[j], v[j], a);
     }
   }
+  return a;
+}
+
+// out[t] = the local partial of token t (bf16 and / or fp32).
+__global__ void __launch_bounds__(256) moe_finalize_kernel(float* __restrict__ part, int round_part,
+                                                           const float* __restrict__ w,
+                                                           const int* __restrict__ idx, int R, int topk, int Nout,
+                                                           int e_begin, int e_end, bf16* __restrict__ out,
+                                                           float* __restrict__ out_f32) {
+  pdl_wait();
+  pdl_trigger();
+  const int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+  if (i >= static_cast<int64_t>(R) * Nout) return;
+  const int t = static_cast<int>(i / Nout), n = static_cast<int>(i % Nout);
+  const float a = local_partial(part, round_part, w, idx, t, n, topk, Nout, e_begin, e_end);
   if (out) out[i] = __float2bfloat16(a);
   if (out_f32) out_f32[i] = a;
+}
+
+// Expert-sharded finalize fused with the all-reduce over NVLink peer memory (no NCCL): CTA c owns
+// a slice of the R x Nout outputs on every rank.  It writes this rank's partials of its slice into
+// this rank's peer-visible buffer (half e & 1 of it, e = the CTA's call count), publishes e to its
+// flag word on every peer (system-scope release), waits for every peer's e (acquire; bounded,
+// status bit on timeout), then sums the slice of all ranks' partials in rank order -- the same
+// order on every rank, so all ranks get identical bits -- and writes bf16.  A peer reads a buffer
+// half at call e only after both ranks finished call e - 1, so alternating halves keeps the next
+// call's writes off data still being read.  The call counters advance in device memory, so a
+// replayed CUDA graph stays in step.
+__device__ __forceinline__ void st_release_sys(uint32_t* p, uint32_t v) {
+  asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+__device__ __forceinline__ uint32_t ld_acquire_sys(const uint32_t* p) {
+  uint32_t v;
+  asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+// rank q's flag words: after its two halves of partials
+__device__ __forceinline__ uint32_t* peer_flags(const PeerReduce& pr, int q) {
+  return reinterpret_cast<uint32_t*>(pr.bufs[q] + 2 * pr.stride);
+}
+
+__global__ void __launch_bounds__(256) moe_finalize_allreduce_kernel(float* __restrict__ part, int round_part,
+                                                                     const float* __restrict__ w,
+                                                                     const int* __restrict__ idx, int R, int topk,
+                                                                     int Nout, int e_begin, int e_end, PeerReduce pr,
+                                                                     bf16* __restrict__ out) {
+  __shared__ uint32_t s_e;
+  __shared__ int s_ok;
+  pdl_wait();
+  pdl_trigger();
+  const int c = blockIdx.x, tid = threadIdx.x;
+  const int64_t n = static_cast<int64_t>(R) * Nout;
+  const int64_t i0 = static_cast<int64_t>(c) * n / gridDim.x, i1 = static_cast<int64_t>(c + 1) * n / gridDim.x;
+  if (tid == 0) {
+    s_e = __ldcg(pr.epoch + c) + 1u;
+    s_ok = 1;
+  }
+  __syncthreads();
+  const uint32_t e = s_e;
+  const int64_t half = static_cast<int64_t>(e & 1u) * pr.stride;
+  float* mine = pr.bufs[pr.rank] + half;
+  for (int64_t i = i0 + tid; i < i1; i += blockDim.x) {
+    const int t = static_cast<int>(i / Nout), col = static_cast<int>(i % Nout);
+    mine[i] = local_partial(part, round_part, w, idx, t, col, topk, Nout, e_begin, e_end);
+  }
+  __syncthreads();
+  if (tid == 0) {
+    __threadfence_system();  // this CTA's partials are visible to the peers before its flag
+    for (int q = 0; q < pr.world; ++q)
+      if (q != pr.rank) st_release_sys(peer_flags(pr, q) + c * pr.world + pr.rank, e);
+    const unsigned long long t0 = globaltimer();
+    for (int q = 0; q < pr.world && s_ok; ++q) {
+      if (q == pr.rank) continue;
+      const uint32_t* f = peer_flags(pr, pr.rank) + c * pr.world + q;
+      while (static_cast<int>(ld_acquire_sys(f) - e) < 0) {
+        if (globaltimer() - t0 > kWaitLimitNs) {
+          set_status(kStatusGridWait);
+          s_ok = 0;
+          break;
+        }
+      }
+    }
+    pr.epoch[c] = e;
+  }
+  __syncthreads();
+  if (!s_ok) return;
+  for (int64_t i = i0 + tid; i < i1; i += blockDim.x) {
+    float s = 0.f;
+    for (int q = 0; q < pr.world; ++q) s += q == pr.rank ? mine[i] : __ldcg(pr.bufs[q] + half + i);
+    out[i] = __float2bfloat16(s);
+  }
 }
 
 template <int FC, int TPR, int SPT>
@@ -538,6 +620,16 @@ cudaError_t launch_moe_finalize(float* part, int round_part, const float* w, con
   const int64_t n = static_cast<int64_t>(R) * 1024;
   return launch_kernel(moe_finalize_kernel, dim3(static_cast<unsigned>((n + 255) / 256)), dim3(256), 0, cfg, part,
                        round_part, w, idx, R, topk, 1024, e_begin, e_end, out, out_partial);
+}
+
+
+cudaError_t launch_moe_finalize_allreduce(float* part, int round_part, const float* w, const int* idx, int R,
+                                          int topk, int e_begin, int e_end, const PeerReduce& pr, bf16* out,
+                                          const LaunchCfg& cfg) {
+  if (pr.world < 1 || pr.rank < 0 || pr.rank >= pr.world || pr.stride < static_cast<int64_t>(R) * 1024)
+    return cudaErrorInvalidValue;
+  return launch_kernel(moe_finalize_allreduce_kernel, dim3(kPeerReduceCtas), dim3(256), 0, cfg, part, round_part, w,
+                       idx, R, topk, 1024, e_begin, e_end, pr, out);
 }
 
 }  // namespace bolt

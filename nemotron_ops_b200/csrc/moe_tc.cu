@@ -726,6 +726,10 @@ cudaError_t launch_moe_group(const int* idx, int P, int topk, int e_begin, int e
 // round_part: part holds fp32 fc2 sums, rounded to bf16 (and written back) here
 cudaError_t launch_moe_finalize(float* part, int round_part, const float* w, const int* idx, int R, int topk,
                                 int e_begin, int e_end, bf16* out, float* out_partial, const LaunchCfg& cfg);
+// the same, fused with the sum over the ranks' partials through peer memory (moe.cu)
+cudaError_t launch_moe_finalize_allreduce(float* part, int round_part, const float* w, const int* idx, int R,
+                                          int topk, int e_begin, int e_end, const PeerReduce& pr, bf16* out,
+                                          const LaunchCfg& cfg);
 // tcgen05 expert layer (moe_umma.cu): whether it takes a layer, and the launch.  Its CTAs build the
 // expert list from idx themselves; fc1 zeroes part_out when given one (fc2 with split relies on
 // that to split tiles) and writes meta when given meta_out.
@@ -737,7 +741,7 @@ cudaError_t launch_moe_layer_umma(int fmt, int fc, const bf16* x, const int* idx
 cudaError_t launch_moe_verify(int fmt, const bf16* z, const int* idx, const float* w, const uint8_t* fc1_w,
                               const bf16* fc1_s, const uint8_t* fc2_w, const bf16* fc2_s, int R, int E, int I,
                               int topk, int e_begin, int e_end, bf16* out, bf16* h, float* part, int* meta,
-                              float* out_partial, const LaunchCfg& cfg) {
+                              float* out_partial, const LaunchCfg& cfg, const PeerReduce* pr) {
   const int P = R * topk;
   // tcgen05 layers where they apply (int4 / native IQ2_XXS, 128-row tiles), else mma.sync.  The
   // tcgen05 layers build the expert list from idx in every CTA; the grouping kernel (which writes
@@ -768,6 +772,7 @@ cudaError_t launch_moe_verify(int fmt, const bf16* z, const int* idx, const floa
     e = launch_grouped(fmt, false, 2, true, h, meta, idx, fc2_w, fc2_s, nullptr, part, P, R, topk, E, e_begin, e_end,
                        I, 1024, c2);
   if (e != cudaSuccess) return e;
+  if (pr != nullptr) return launch_moe_finalize_allreduce(part, 1, w, idx, R, topk, e_begin, e_end, *pr, out, c2);
   return launch_moe_finalize(part, 1, w, idx, R, topk, e_begin, e_end, out, out_partial, c2);
 }
 

@@ -174,6 +174,35 @@ def moe_verify_shard(z, idx, w, fc1_w, fc1_s, fc2_w, fc2_s, topk: int, iq2: int,
     return out_partial, h, part, meta
 
 
+def moe_verify_shard_allreduce(z, idx, w, fc1_w, fc1_s, fc2_w, fc2_s, topk: int, iq2: int, e_begin: int,
+                               e_end: int, reducer, num_experts: int = None, out=None, outputs=None):
+    """Expert-sharded MoeVerify whose last kernel also sums every rank's partial through peer
+    memory (``reducer``: a :class:`nemotron_ops_b200.sharded.PeerReducer`); returns out bf16
+    [R, 1024], identical on every rank.  Weights and ``outputs`` as for :func:`moe_verify_shard`."""
+    _need(z, idx, w, fc1_w, fc1_s, fc2_w, fc2_s)
+    R = z.shape[0]
+    P = R * topk
+    E = int(num_experts) if num_experts is not None else fc1_w.shape[0]
+    local = fc1_w.shape[0] != E
+    if local and fc1_w.shape[0] != e_end - e_begin:
+        raise RuntimeError("moe_verify_shard_allreduce: local weights must hold exactly experts [e_begin, e_end)")
+    if outputs is None:
+        _, h, part = _moe_outputs(z, fc1_w, topk)
+        meta = torch.empty(1 + P + 8 * P, dtype=torch.int32, device=z.device)
+    else:
+        h, part, meta = outputs
+    if out is None:
+        out = torch.empty(R, 1024, dtype=torch.bfloat16, device=z.device)
+    zs, _k1 = shape_arg(z.shape)
+    w1s, _k2 = shape_arg((E,) + tuple(fc1_w.shape[1:]))
+    wp = [_expert_ptr(t, e_begin) if local else _ptr(t) for t in (fc1_w, fc1_s, fc2_w, fc2_s)]
+    _check(lib().bolt_moe_verify_shard_allreduce(
+        _ptr(z), zs, z.dim(), _ptr(idx), _ptr(w), wp[0], w1s, fc1_w.dim(), wp[1], wp[2], wp[3], int(topk), int(iq2),
+        int(e_begin), int(e_end), _ptr(h), _ptr(part), _ptr(meta), ctypes.c_void_p(reducer.bufs_dev),
+        _ptr(reducer.counters), int(reducer.half), int(reducer.rank), int(reducer.world), _ptr(out), _stream(z)))
+    return out
+
+
 def moe_decode_shard(z, idx, w, fc1_w, fc1_s, fc2_w, fc2_s, topk: int, e_begin: int, e_end: int,
                      num_experts: int = None, out_partial=None, outputs=None):
     """MoeDecode over experts [e_begin, e_end) only; returns (out_partial f32 [R, 1024], h, part).

@@ -14,12 +14,13 @@ computation.
 """
 from __future__ import annotations
 
+import os
 from typing import Callable, Optional
 
 import torch
 import torch.distributed as dist
 
-__all__ = ["expert_range", "ShardedMoeVerify", "ShardedMoeDecode"]
+__all__ = ["expert_range", "ShardedMoeVerify", "ShardedMoeDecode", "PeerReducer"]
 
 
 def expert_range(num_experts: int, rank: int, world: int):
@@ -27,6 +28,33 @@ def expert_range(num_experts: int, rank: int, world: int):
     if world < 1 or not 0 <= rank < world:
         raise ValueError("expert_range: need 0 <= rank < world")
     return rank * num_experts // world, (rank + 1) * num_experts // world
+
+
+class PeerReducer:
+    """Peer-visible buffers of ``bolt_moe_verify_shard_allreduce`` for the ranks of ``group``
+    (CUDA, one process per GPU): torch symmetric memory maps every rank's buffer -- two halves of
+    ``max_rows * 1024`` fp32 partials, then the flag words, zeroed here -- into every peer; the
+    call counters are this rank's.  Only plain peer loads and stores touch it, so torch's NVLink
+    multicast binding is switched off (unless the caller set TORCH_SYMM_MEM_DISABLE_MULTICAST).
+    Create it on every rank (a collective) before stream capture, and make the same sequence of
+    calls on every rank."""
+
+    CTAS = 16  # kPeerReduceCtas of the kernel
+
+    def __init__(self, group=None, max_rows: int = 8, device=None):
+        os.environ.setdefault("TORCH_SYMM_MEM_DISABLE_MULTICAST", "1")
+        import torch.distributed._symmetric_memory as symm_mem
+        device = device if device is not None else torch.device("cuda", torch.cuda.current_device())
+        group = group if group is not None else dist.group.WORLD
+        world = dist.get_world_size(group)
+        self.half = int(max_rows) * 1024
+        self.buf = symm_mem.empty(2 * self.half + self.CTAS * world, dtype=torch.float32, device=device)
+        self.buf.zero_()
+        torch.cuda.synchronize(device)
+        self.handle = symm_mem.rendezvous(self.buf, group)
+        self.rank, self.world = self.handle.rank, self.handle.world_size
+        self.bufs_dev = self.handle.buffer_ptrs_dev
+        self.counters = torch.zeros(self.CTAS, dtype=torch.int32, device=device)
 
 
 class ShardedMoeVerify:
@@ -67,6 +95,14 @@ class ShardedMoeVerify:
     def partial(self, z, idx, w, weights) -> torch.Tensor:
         """fp32 [R, 1024]: sum over this rank's pairs of w * part."""
         return self.shard_fn(z, idx, w, weights, self.e_begin, self.e_end)
+
+    def fused(self, z, idx, w, weights, reducer: "PeerReducer", out=None, outputs=None) -> torch.Tensor:
+        """As ``__call__``, with the partials summed through peer memory inside the op's last
+        kernel (``bolt_moe_verify_shard_allreduce``) instead of an NCCL all-reduce and a cast."""
+        from . import ops
+        return ops.moe_verify_shard_allreduce(z, idx, w, *weights, topk=self.topk, iq2=self.iq2, e_begin=self.e_begin,
+                                              e_end=self.e_end, reducer=reducer, num_experts=self.num_experts,
+                                              out=out, outputs=outputs)
 
     def __call__(self, z, idx, w, weights) -> torch.Tensor:
         """bf16 [R, 1024] MoeVerify output, identical on every rank."""
