@@ -349,7 +349,9 @@ def max_over_ranks(v, world):
 
 
 def sharded_moe_measure(world, rank, device, iq2=0, E=304, I=2304, R=8, topk=8, iters=30, warmup=5):
-    """Expert-sharded MoeVerify step: local shard kernels + fp32 NCCL all-reduce + bf16 cast.
+    """Expert-sharded MoeVerify step, two ways: the fused op (shard kernels, then a finalize
+    kernel that sums the ranks' partials through NVLink peer memory) and the NCCL path (shard
+    kernels, fp32 NCCL all-reduce, bf16 cast); plus the shard kernels alone.
 
     Every rank routes the same seeded inputs and holds only its own experts' weights (rotated
     copies larger than 3x L2).  The steps are replayed from a CUDA graph; times are CUDA events
@@ -358,7 +360,7 @@ def sharded_moe_measure(world, rank, device, iq2=0, E=304, I=2304, R=8, topk=8, 
 
     from nemotron_ops_b200 import ops
     from nemotron_ops_b200 import workloads as W
-    from nemotron_ops_b200.sharded import ShardedMoeVerify
+    from nemotron_ops_b200.sharded import PeerReducer, ShardedMoeVerify
 
     r = W.moe_route(R=R, E=E, K=4096, seed=0, device=device)
     idx, w, _ = ops.MoeRoute(r["x"], r["gate_w"], r["bias"], topk, 5.0)
@@ -382,18 +384,24 @@ def sharded_moe_measure(world, rank, device, iq2=0, E=304, I=2304, R=8, topk=8, 
                torch.empty(P, 1024, dtype=torch.float32, device=device),
                torch.empty(1 + P + 8 * P, dtype=torch.int32, device=device))
 
-    def run(i, reduce=True):
+    reducer = PeerReducer(max_rows=R, device=device) if world > 1 else None
+
+    def run(i, mode):
+        if mode == "peer":
+            ops.moe_verify_shard_allreduce(z, idx, w, *weights[i % copies], topk=topk, iq2=iq2, e_begin=e0,
+                                           e_end=e1, reducer=reducer, num_experts=E, out=out, outputs=scratch)
+            return
         ops.moe_verify_shard(z, idx, w, *weights[i % copies], topk=topk, iq2=iq2, e_begin=e0, e_end=e1,
                              num_experts=E, out_partial=out_p, outputs=scratch)
-        if reduce:
+        if mode == "nccl":
             dist.all_reduce(out_p, op=dist.ReduceOp.SUM)
         ops.f32_to_bf16(out_p, out=out)
 
-    def timed(reduce):
+    def timed(mode):
         # CUDA graph of `iters` steps (shard kernels, NCCL all-reduce, cast) over rotated weights,
         # like the single-GPU legs; every rank captures and replays the same collectives
         for i in range(warmup):
-            run(i, reduce)
+            run(i, mode)
         torch.cuda.synchronize()
         barrier(world)
         side = torch.cuda.Stream()
@@ -402,7 +410,7 @@ def sharded_moe_measure(world, rank, device, iq2=0, E=304, I=2304, R=8, topk=8, 
         with torch.cuda.stream(side):
             with torch.cuda.graph(g):
                 for i in range(iters):
-                    run(i, reduce)
+                    run(i, mode)
         torch.cuda.current_stream().wait_stream(side)
         g.replay()
         torch.cuda.synchronize()
@@ -417,12 +425,15 @@ def sharded_moe_measure(world, rank, device, iq2=0, E=304, I=2304, R=8, topk=8, 
         barrier(world)
         return us
 
-    us_total = timed(True)
-    us_compute = timed(False)
+    us_nccl = timed("nccl")
+    us_compute = timed("local")
+    us_total = timed("peer") if reducer is not None else us_nccl
     uniq_all = max_over_ranks(float(local_uniq), world)
     return {"workload": f"sharded MoeVerify {'iq2=2' if iq2 else 'int4'} R={R} E={E} k={topk} I={I} over {world} GPUs",
-            "us_per_call": round(us_total, 2), "us_shard_compute": round(us_compute, 2),
-            "us_allreduce_and_cast": round(us_total - us_compute, 2),
+            "us_per_call": round(us_nccl, 2), "path": "shard kernels, NCCL all-reduce, cast (the default)",
+            "us_shard_compute": round(us_compute, 2), "us_allreduce_and_cast": round(us_nccl - us_compute, 2),
+            "us_per_call_fused_peer_reduction": round(us_total, 2),
+            "us_exchange_fused_peer_reduction": round(us_total - us_compute, 2),
             "max_local_unique_experts": int(uniq_all), "bytes_max_rank": int(uniq_all * per_expert),
             "experts_per_rank": e1 - e0}
 
