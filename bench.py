@@ -113,7 +113,9 @@ def _gemv_workload(kind, R, N, K, iq2=0):
     return build
 
 
-def _moe_workload(op_name, R, iq2=0, E=304, I=2304, topk=8):
+def _moe_workload(op_name, R, iq2=0, E=304, I=2304, topk=8, route=False):
+    """One MoE layer per call; with route, MoeRoute and the layer run back to back in the same
+    captured sequence (router gate weights, one distinct copy per expert set)."""
     from nemotron_ops_b200 import ops
     from nemotron_ops_b200 import workloads as W
 
@@ -130,9 +132,16 @@ def _moe_workload(op_name, R, iq2=0, E=304, I=2304, topk=8):
         e0 = sets[0]
         per_expert = sum(e0[k][0].numel() * e0[k].element_size() for k in ("fc1_w", "fc1_s", "fc2_w", "fc2_s"))
         nbytes = uniq * per_expert + R * 1024 * 2 + R * topk * 8 + R * 1024 * 2
+        if route:  # + gate weights, bias, x, scores, idx/w
+            nbytes += E * 4096 * 2 + E * 4 + R * 4096 * 2 + R * E * 4 + R * topk * 8
+            for d in sets:
+                d["gate_w"] = r["gate_w"].clone()
 
         def op(d, zz):
-            a = [zz, idx, w, d["fc1_w"], d["fc1_s"], d["fc2_w"], d["fc2_s"]]
+            ii, ww = idx, w
+            if route:
+                ii, ww, _ = ops.MoeRoute(r["x"], d["gate_w"], r["bias"], topk, 5.0)
+            a = [zz, ii, ww, d["fc1_w"], d["fc1_s"], d["fc2_w"], d["fc2_s"]]
             if op_name == "MoeDecode":
                 return ops.MoeDecode(*a, topk=topk)[0]
             return ops.MoeVerify(*a, topk=topk, iq2=iq2)[0]
@@ -154,16 +163,49 @@ def _moe_workload(op_name, R, iq2=0, E=304, I=2304, topk=8):
             c = [t.cpu() for t in (z, idx, w, e0["fc1_w"], e0["fc1_s"], e0["fc2_w"], e0["fc2_s"])]
             rows = max(1, n // topk)
             args = [c[0][:rows], c[1][:rows], c[2][:rows]] + c[3:]
+            if route:
+                O.moe_route(r["x"][:rows].cpu(), r["gate_w"].cpu(), r["bias"].cpu(), topk, 5.0)
             if op_name == "MoeDecode":
                 O.moe_decode(*args, topk=topk, fp32=True)
             else:
                 O.moe_verify(*args, topk=topk, iq2=iq2, fp32=True)
             return nbytes * rows / R
 
-        kern = 3 if op_name == "MoeDecode" else 4
-        return dict(calls=calls, bytes=nbytes, kernels=2 if op_name == "MoeDecode" else kern, h2d=R * 1024 * 2,
+        kern = 3 + (2 if route else 0)  # fc1, fc2, finalize (+ router logits, top-k)
+        return dict(calls=calls, bytes=nbytes, kernels=kern, h2d=R * 1024 * 2,
                     d2h=R * 1024 * 2, e2e=e2e, cpu=cpu, cpu_sample=R * topk, dtype="f32" if op_name == "MoeDecode"
                     else "bf16", unique_experts=uniq, kernel="moe_tc_kernel")
+    return build
+
+
+def _route_workload(R, E=304, K=4096, topk=8):
+    """MoeRoute alone: the gate weights [E, K] bf16 are the stream (2.5 MB per call)."""
+    from nemotron_ops_b200 import ops
+    from nemotron_ops_b200 import workloads as W
+
+    def build(device, copies):
+        r = W.moe_route(R=R, E=E, K=K, seed=0, device=device)
+        gates = [(torch.randn(E, K, generator=torch.Generator(device=device).manual_seed(20 + c), device=device)
+                  * 0.02).to(torch.bfloat16) for c in range(copies)]
+        nbytes = E * K * 2 + E * 4 + R * K * 2 + R * E * 4 + R * topk * 8
+        calls = [(lambda gw=gw: ops.MoeRoute(r["x"], gw, r["bias"], topk, 5.0)) for gw in gates]
+        pin = str(device) != "cpu"
+        xh = r["x"].cpu().pin_memory() if pin else r["x"]
+        ih = torch.empty(R, topk, dtype=torch.int32).pin_memory() if pin else None
+        xd = torch.empty_like(r["x"])
+
+        def e2e(i):
+            xd.copy_(xh, non_blocking=True)
+            idx, w, _ = ops.MoeRoute(xd, gates[i], r["bias"], topk, 5.0)
+            ih.copy_(idx, non_blocking=True)
+
+        def cpu(_sample):
+            import oracle as O
+            O.moe_route(r["x"].cpu(), gates[0].cpu(), r["bias"].cpu(), topk, 5.0)
+            return nbytes
+
+        return dict(calls=calls, bytes=nbytes, kernels=2, h2d=R * K * 2, d2h=R * topk * 4, e2e=e2e, cpu=cpu,
+                    cpu_sample=1, dtype="f32", kernel="router_logits_kernel")
     return build
 
 
@@ -260,6 +302,12 @@ WORKLOADS = {
     "moe_decode_r1": ("MoeDecode R=1 E=304 k=8 I=2304 (configs[3])", _moe_workload("MoeDecode", 1)),
     "moe_verify_r8": ("MoeVerify int4 R=8 E=304 k=8 I=2304 (configs[4])", _moe_workload("MoeVerify", 8)),
     "moe_verify_iq2n_r8": ("MoeVerify iq2=2 R=8 E=304 k=8 I=2304 (configs[4])", _moe_workload("MoeVerify", 8, iq2=2)),
+    "moe_route_r1": ("MoeRoute R=1 E=304 K=4096 topk=8 (configs[3] routing)", _route_workload(1)),
+    "moe_route_r8": ("MoeRoute R=8 E=304 K=4096 topk=8 (configs[4] routing)", _route_workload(8)),
+    "route_moe_decode_r1": ("MoeRoute + MoeDecode R=1 E=304 k=8 I=2304 in one captured sequence (configs[3])",
+                            _moe_workload("MoeDecode", 1, route=True)),
+    "route_moe_verify_r8": ("MoeRoute + MoeVerify int4 R=8 E=304 k=8 I=2304 in one captured sequence (configs[4])",
+                            _moe_workload("MoeVerify", 8, route=True)),
     "relu2": ("Relu2 x bf16 [8, 4194304] (not a BASELINE config; HBM stream)", _relu2_workload(8, 4194304)),
     "mamba_step_r1": ("MambaStep R=1 heads=128 ng=8 (not a BASELINE config; reference test size)",
                       _mamba_workload(1, False)),

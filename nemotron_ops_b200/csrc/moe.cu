@@ -2,7 +2,7 @@
 // src/bolt_ops.cu:359-472, :552-587, :1084-1112); the expert GEMMs are in moe_tc.cu.
 //
 // MoeRoute: the fp32 router logits are one streaming dot per expert spread over all SMs (each
-// warp reads one gate row once and applies it to every activation row); the selection is one
+// gate row is read once and applied to every activation row); the selection is one
 // warp per row: `topk` rounds of warp arg-max over score + bias with ties to the lower index.
 //
 // MoeVerify grouping: one CTA writes the reference's `meta` layout (unique experts in
@@ -18,43 +18,99 @@ namespace {
 // =======================================================================================
 // MoeRoute
 // =======================================================================================
-// one warp per expert; lanes stride over K in 16-byte vectors; every activation row reuses
-// the gate row held in registers (K <= 8192 -> 32 x 16 B per lane at most)
-template <int RMAX>
-__global__ void __launch_bounds__(128) router_logits_kernel(const bf16* __restrict__ x, const bf16* __restrict__ gw,
-                                                            int R, int K, int E, float* __restrict__ scores) {
+// Logits: two gate rows per CTA, four warps (128 lanes) per row.  K is walked in passes of 4096
+// (512 16-byte vectors per row); in a pass lane t of a row loads vectors t, t+128, t+256, t+384,
+// all issued before the first use, so one pass of the whole grid puts the full 2.5 MB gate of
+// E = 304, K = 4096 in flight at once.  The pass's activation rows (at most 8 x 4096 bf16 = 64 KB)
+// are staged in shared memory once per CTA instead of being re-read from L2 by every warp.  The
+// row's four warp sums are added in warp order, so results do not depend on scheduling.
+constexpr int kRouteExperts = 2;                            // gate rows per CTA
+constexpr int kRouteRowLanes = 128;                         // lanes per gate row
+constexpr int kRouteVec = 4;                                // 16-byte gate vectors per lane and pass
+constexpr int kRoutePassVec = kRouteRowLanes * kRouteVec;   // 512 vectors = 4096 k per pass
+constexpr int kRouteThreads = kRouteExperts * kRouteRowLanes;
+
+__device__ __forceinline__ void dot_bf16x8(const uint4& a, const uint4& b, float& acc) {
+  const uint32_t aa[4] = {a.x, a.y, a.z, a.w}, bb[4] = {b.x, b.y, b.z, b.w};
+#pragma unroll
+  for (int q = 0; q < 4; ++q) {
+    acc = fmaf(__uint_as_float(aa[q] << 16), __uint_as_float(bb[q] << 16), acc);
+    acc = fmaf(__uint_as_float(aa[q] & 0xFFFF0000u), __uint_as_float(bb[q] & 0xFFFF0000u), acc);
+  }
+}
+
+template <int RB>  // activation rows per block of rows (1 for R = 1, else 8)
+__global__ void __launch_bounds__(kRouteThreads, 2)
+    router_logits_kernel(const bf16* __restrict__ x, const bf16* __restrict__ gw, int R, int K, int E, int early,
+                         float* __restrict__ scores) {
+  extern __shared__ __align__(16) uint4 xs[];  // [RB][kRoutePassVec]
+  __shared__ float red[kRouteThreads / 32][RB];
   pdl_trigger();
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int e = blockIdx.x * 4 + warp;
-  pdl_wait();
-  if (e >= E) return;
-  const bf16* wr = gw + static_cast<int64_t>(e) * K;
-  const int nv = K >> 8;  // 16-byte vectors per lane (K % 256 == 0)
-  for (int r0 = 0; r0 < R; r0 += RMAX) {
-    float acc[RMAX];
+  const int e = blockIdx.x * kRouteExperts + (warp >> 2);
+  const int t = (warp & 3) * 32 + lane;
+  const int V = K >> 3;  // 16-byte vectors per row (K % 256 == 0)
+  const uint4* wr = reinterpret_cast<const uint4*>(gw) + static_cast<int64_t>(e < E ? e : E - 1) * V;
+  const uint4* xv = reinterpret_cast<const uint4*>(x);
+  bool waited = false;
+  for (int r0 = 0; r0 < R; r0 += RB) {
+    const int rows = min(RB, R - r0);
+    float acc[RB];
 #pragma unroll
-    for (int r = 0; r < RMAX; ++r) acc[r] = 0.f;
-    for (int v = 0; v < nv; ++v) {
-      const int k = (v * 32 + lane) * 8;
-      const uint4 wv = __ldg(reinterpret_cast<const uint4*>(wr + k));
-      const uint32_t ww[4] = {wv.x, wv.y, wv.z, wv.w};
+    for (int r = 0; r < RB; ++r) acc[r] = 0.f;
+    for (int base = 0; base < V; base += kRoutePassVec) {
+      const int pv = min(kRoutePassVec, V - base);
+      if (!early && !waited) {  // the gate may be written upstream: wait before reading it
+        pdl_wait();
+        waited = true;
+      }
+      uint4 wv[kRouteVec];
 #pragma unroll
-      for (int r = 0; r < RMAX; ++r) {
-        if (r0 + r < R) {
-          const uint4 xv = __ldg(reinterpret_cast<const uint4*>(x + static_cast<int64_t>(r0 + r) * K + k));
-          const uint32_t xx[4] = {xv.x, xv.y, xv.z, xv.w};
+      for (int j = 0; j < kRouteVec; ++j) {
+        const int v = t + j * kRouteRowLanes;
+        wv[j] = v < pv ? __ldg(wr + base + v) : make_uint4(0u, 0u, 0u, 0u);
+      }
+      if (!waited) {
+        pdl_wait();
+        waited = true;
+      }
+      __syncthreads();  // the previous pass has finished reading xs
 #pragma unroll
-          for (int q = 0; q < 4; ++q) {
-            acc[r] = fmaf(__uint_as_float(ww[q] << 16), __uint_as_float(xx[q] << 16), acc[r]);
-            acc[r] = fmaf(__uint_as_float(ww[q] & 0xFFFF0000u), __uint_as_float(xx[q] & 0xFFFF0000u), acc[r]);
+      for (int r = 0; r < RB; ++r) {
+        if (r < rows) {
+#pragma unroll
+          for (int j = 0; j < kRoutePassVec / kRouteThreads; ++j) {
+            const int v = threadIdx.x + j * kRouteThreads;
+            if (v < pv) xs[r * kRoutePassVec + v] = __ldg(xv + static_cast<int64_t>(r0 + r) * V + base + v);
+          }
+        }
+      }
+      __syncthreads();
+#pragma unroll
+      for (int r = 0; r < RB; ++r) {
+        if (r < rows) {
+#pragma unroll
+          for (int j = 0; j < kRouteVec; ++j) {
+            const int v = t + j * kRouteRowLanes;
+            if (v < pv) dot_bf16x8(wv[j], xs[r * kRoutePassVec + v], acc[r]);
           }
         }
       }
     }
 #pragma unroll
-    for (int r = 0; r < RMAX; ++r) {
+    for (int r = 0; r < RB; ++r) {
       const float a = warp_sum(acc[r]);
-      if (lane == 0 && r0 + r < R) scores[static_cast<int64_t>(r0 + r) * E + e] = 1.0f / (1.0f + expf(-a));
+      if (lane == 0) red[warp][r] = a;
+    }
+    __syncthreads();
+    if (threadIdx.x < kRouteExperts * RB) {
+      const int eo = threadIdx.x / RB, r = threadIdx.x % RB;
+      const int ee = blockIdx.x * kRouteExperts + eo;
+      if (ee < E && r < rows) {
+        const float* q = &red[eo * 4][r];
+        const float a = ((q[0] + q[RB]) + q[2 * RB]) + q[3 * RB];
+        scores[static_cast<int64_t>(r0 + r) * E + ee] = 1.0f / (1.0f + expf(-a));
+      }
     }
   }
 }
@@ -581,9 +637,20 @@ cudaError_t dispatch_seg(SegParams& p, int grid, const LaunchCfg& cfg) {
 
 cudaError_t launch_moe_route(const bf16* x, const bf16* gate_w, const float* bias, int R, int K, int E, int topk,
                              float scale, int* idx, float* w, float* scores, const LaunchCfg& cfg) {
-  const unsigned blocks = static_cast<unsigned>((E + 3) / 4);
-  cudaError_t e = R <= 1 ? launch_kernel(router_logits_kernel<1>, dim3(blocks), dim3(128), 0, cfg, x, gate_w, R, K, E, scores)
-                         : launch_kernel(router_logits_kernel<8>, dim3(blocks), dim3(128), 0, cfg, x, gate_w, R, K, E, scores);
+  const unsigned blocks = static_cast<unsigned>((E + kRouteExperts - 1) / kRouteExperts);
+  const int early = cfg.early_weights ? 1 : 0;
+  cudaError_t e;
+  if (R <= 1) {
+    e = launch_kernel(router_logits_kernel<1>, dim3(blocks), dim3(kRouteThreads), kRoutePassVec * sizeof(uint4), cfg,
+                      x, gate_w, R, K, E, early, scores);
+  } else {
+    constexpr size_t smem = 8 * kRoutePassVec * sizeof(uint4);
+    e = cudaFuncSetAttribute(router_logits_kernel<8>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             static_cast<int>(smem));
+    if (e == cudaSuccess)
+      e = launch_kernel(router_logits_kernel<8>, dim3(blocks), dim3(kRouteThreads), smem, cfg, x, gate_w, R, K, E,
+                        early, scores);
+  }
   if (e != cudaSuccess) return e;
   LaunchCfg c2 = cfg;
   c2.pdl = true;  // same op: the selection waits for the logits with griddepcontrol.wait

@@ -203,3 +203,37 @@ def test_moe_verify_graph_capture():
     g.replay()
     torch.cuda.synchronize()
     assert torch.equal(out, ref)
+
+
+@pytest.mark.parametrize("op,R", [("MoeDecode", 1), ("MoeVerify", 8)])
+def test_route_then_moe_one_graph(op, R):
+    # MoeRoute and the MoE layer captured back to back in one CUDA graph (the launches chain by
+    # programmatic dependent launch); replays equal the eager sequence and the oracle
+    E, I, topk = 64, 512, 8
+    r = W.moe_route(R=R, E=E, K=4096, seed=11)
+    ex = W.moe_experts(E=E, I=I, seed=11)
+    z = W.moe_latent(R=R, seed=11)
+    fn = ops.MoeDecode if op == "MoeDecode" else ops.MoeVerify
+
+    def step():
+        idx, w, _ = ops.MoeRoute(r["x"], r["gate_w"], r["bias"], topk, 5.0)
+        return (idx, w) + tuple(fn(z, idx, w, ex["fc1_w"], ex["fc1_s"], ex["fc2_w"], ex["fc2_s"], topk=topk))
+
+    s = torch.cuda.Stream()
+    s.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(s):
+        ref = [t.clone() for t in step()]
+    torch.cuda.current_stream().wait_stream(s)
+    torch.cuda.synchronize()
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g):
+        got = step()
+    for _ in range(3):
+        g.replay()
+    torch.cuda.synchronize()
+    for a, b in zip(got, ref):
+        assert torch.equal(a, b)
+    idx, w = got[0], got[1]
+    _check_route(r["x"], r["gate_w"], r["bias"], topk, 5.0)
+    ins = [z, idx, w, ex["fc1_w"], ex["fc1_s"], ex["fc2_w"], ex["fc2_s"]]
+    _check_moe(op, ins, topk, on_device=True)
