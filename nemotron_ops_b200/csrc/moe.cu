@@ -74,16 +74,23 @@ __global__ void __launch_bounds__(kRouteThreads, 2)
         pdl_wait();
         waited = true;
       }
+      // every activation load of the pass is issued before the first shared-memory store
+      constexpr int XJ = kRoutePassVec / kRouteThreads;
+      uint4 xr[RB][XJ];
+#pragma unroll
+      for (int r = 0; r < RB; ++r) {
+#pragma unroll
+        for (int j = 0; j < XJ; ++j) {
+          const int v = threadIdx.x + j * kRouteThreads;
+          xr[r][j] = (r < rows && v < pv) ? __ldg(xv + static_cast<int64_t>(r0 + r) * V + base + v)
+                                          : make_uint4(0u, 0u, 0u, 0u);
+        }
+      }
       __syncthreads();  // the previous pass has finished reading xs
 #pragma unroll
       for (int r = 0; r < RB; ++r) {
-        if (r < rows) {
 #pragma unroll
-          for (int j = 0; j < kRoutePassVec / kRouteThreads; ++j) {
-            const int v = threadIdx.x + j * kRouteThreads;
-            if (v < pv) xs[r * kRoutePassVec + v] = __ldg(xv + static_cast<int64_t>(r0 + r) * V + base + v);
-          }
-        }
+        for (int j = 0; j < XJ; ++j) xs[r * kRoutePassVec + threadIdx.x + j * kRouteThreads] = xr[r][j];
       }
       __syncthreads();
 #pragma unroll
