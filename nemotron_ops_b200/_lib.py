@@ -62,6 +62,17 @@ def last_error() -> str:
     return msg.decode() if msg else ""
 
 
+_SHAPES: dict = {}
+
+
 def shape_arg(shape):
-    arr = (ctypes.c_int64 * max(1, len(shape)))(*[int(s) for s in shape])
-    return ctypes.cast(arr, _S), arr
+    """(int64_t* view, owning array) for a shape.  Shapes repeat from call to call, so the
+    read-only arrays are cached (building one costs several microseconds per call)."""
+    key = tuple(int(s) for s in shape)
+    hit = _SHAPES.get(key)
+    if hit is None:
+        arr = (ctypes.c_int64 * max(1, len(key)))(*key)
+        hit = (ctypes.cast(arr, _S), arr)
+        if len(_SHAPES) < 4096:
+            _SHAPES[key] = hit
+    return hit

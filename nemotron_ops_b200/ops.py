@@ -22,11 +22,13 @@ FMT_Q8, FMT_Q4, FMT_NVFP4, FMT_IQ2_LUT, FMT_IQ2_NATIVE = 0, 1, 2, 3, 4
 
 
 def _ptr(t):
-    return ctypes.c_void_p(t.data_ptr()) if t is not None else ctypes.c_void_p(0)
+    # plain ints: ctypes converts them for c_void_p parameters without a wrapper object per call
+    return t.data_ptr() if t is not None else None
 
 
 def _stream(t):
-    return ctypes.c_void_p(torch.cuda.current_stream(t.device).cuda_stream)
+    # the raw cudaStream_t of torch's current stream on t's device (as current_stream().cuda_stream)
+    return torch._C._cuda_getCurrentRawStream(t.device.index)
 
 
 def _need(*tensors):
