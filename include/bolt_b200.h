@@ -266,6 +266,15 @@ BOLT_API int bolt_relu2(const void* x, const int64_t* x_shape, int x_rank, void*
 BOLT_API int bolt_f32_to_bf16(const void* in, void* out, int64_t n, void* stream);
 
 /*
+ * Stream-ordered copy of `bytes` bytes between host and device memory, either direction (one
+ * cudaMemcpyAsync with the direction taken from the pointers; pinned host memory makes it
+ * asynchronous).  No reference counterpart: the copy a host caller (ORT, a C or Go binding)
+ * issues around an op, exposed so that bindings without a CUDA runtime of their own can stage
+ * HOST buffers through this library.
+ */
+BOLT_API int bolt_memcpy_async(void* dst, const void* src, int64_t bytes, void* stream);
+
+/*
  * Debug / contract check: dequantise N weight rows of K values into f32 [N, K] with the
  * kernels' own decoders.  fmt: 0 = Q8, 1 = Q4 int4, 2 = NVFP4 (e2m1 * e4m3, no global
  * scale), 3 = IQ2 LUT codes, 4 = native IQ2_XXS.  exact = 1 (Q8 / Q4 only) gives the

@@ -36,6 +36,7 @@ SIGNATURES = {
                                _F, _P, _P, _P, _P, _P, _P]),
     "bolt_relu2": (_I, [_P, _S, _I, _P, _P]),
     "bolt_f32_to_bf16": (_I, [_P, _P, _L, _P]),
+    "bolt_memcpy_async": (_I, [_P, _P, _L, _P]),
     "bolt_dequant": (_I, [_I, _I, _P, _P, _L, _L, _P, _P]),
 }
 

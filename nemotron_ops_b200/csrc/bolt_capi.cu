@@ -473,6 +473,16 @@ int bolt_f32_to_bf16(const void* in, void* out, int64_t n, void* stream) {
   });
 }
 
+int bolt_memcpy_async(void* dst, const void* src, int64_t bytes, void* stream) {
+  return guarded([&] {
+    require(bytes >= 0, "bolt_memcpy_async: negative size");
+    if (bytes == 0) return;
+    require(dst != nullptr && src != nullptr, "bolt_memcpy_async: null buffer");
+    check_launch(cudaMemcpyAsync(dst, src, static_cast<size_t>(bytes), cudaMemcpyDefault,
+                                 static_cast<cudaStream_t>(stream)));
+  });
+}
+
 int bolt_dequant(int fmt, int exact, const void* w, const void* scales, int64_t N, int64_t K, void* out, void* stream) {
   return guarded([&] {
     require(fmt >= 0 && fmt <= 4, "bolt_dequant: unknown format");

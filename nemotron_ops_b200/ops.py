@@ -15,7 +15,7 @@ import torch
 from ._lib import last_error, lib, shape_arg
 
 __all__ = ["Nvfp4Gemv", "Q8Gemv", "Q4Gemv", "MoeRoute", "MoeDecode", "MoeVerify", "moe_verify_shard",
-           "f32_to_bf16", "dequant", "set_launch_options", "device_status", "FMT_Q8", "FMT_Q4", "FMT_NVFP4",
+           "f32_to_bf16", "copy_async", "dequant", "set_launch_options", "device_status", "FMT_Q8", "FMT_Q4", "FMT_NVFP4",
            "FMT_IQ2_LUT", "FMT_IQ2_NATIVE"]
 
 FMT_Q8, FMT_Q4, FMT_NVFP4, FMT_IQ2_LUT, FMT_IQ2_NATIVE = 0, 1, 2, 3, 4
@@ -293,6 +293,15 @@ def f32_to_bf16(t, out=None):
         out = torch.empty(t.shape, dtype=torch.bfloat16, device=t.device)
     _check(lib().bolt_f32_to_bf16(_ptr(t), _ptr(out), t.numel(), _stream(t)))
     return out
+
+
+def copy_async(dst, src):
+    """dst <- src between host (pinned for an asynchronous copy) and device memory, ordered on
+    the current stream of whichever tensor is on the GPU (one cudaMemcpyAsync)."""
+    if dst.nbytes != src.nbytes or not dst.is_contiguous() or not src.is_contiguous():
+        raise RuntimeError("copy_async: contiguous tensors of the same byte size")
+    _check(lib().bolt_memcpy_async(_ptr(dst), _ptr(src), dst.nbytes, _stream(dst if dst.is_cuda else src)))
+    return dst
 
 
 def dequant(fmt: int, w, scales, N: int, K: int, exact: bool = False):

@@ -158,3 +158,12 @@ def test_mamba_validation(kw, msg):
     args.update(kw)
     rc, err = _call_mamba(**args)
     assert rc != 0 and msg in err, err
+
+
+def test_memcpy_async_validation():
+    lib = _lib.lib()
+    assert lib.bolt_memcpy_async(NULL, NULL, 0, NULL) == 0  # nothing to copy: no CUDA call
+    assert lib.bolt_memcpy_async(NULL, NULL, -1, NULL) != 0
+    assert b"negative size" in lib.bolt_last_error()
+    assert lib.bolt_memcpy_async(NULL, NULL, 16, NULL) != 0
+    assert b"null buffer" in lib.bolt_last_error()
