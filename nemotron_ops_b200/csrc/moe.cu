@@ -2,8 +2,8 @@
 // src/bolt_ops.cu:359-472, :552-587, :1084-1112); the expert GEMMs are in moe_tc.cu.
 //
 // MoeRoute: the fp32 router logits are one streaming dot per expert spread over all SMs (each
-// gate row is read once and applied to every activation row); the selection is one
-// warp per row: `topk` rounds of warp arg-max over score + bias with ties to the lower index.
+// gate row is read once and applied to every activation row); the selection sorts packed
+// (score + bias, expert) keys per warp and merges the sorted runs in a tree (one CTA per row).
 //
 // MoeVerify grouping: one CTA writes the reference's `meta` layout (unique experts in
 // first-occurrence order and each expert's (token -> pair) map), restricted to a shard's expert
@@ -122,55 +122,88 @@ __global__ void __launch_bounds__(kRouteThreads, 2)
   }
 }
 
-// one warp per row, E <= 512 (16 candidates per lane)
-__global__ void __launch_bounds__(32) router_topk_kernel(const float* __restrict__ scores, const float* __restrict__ bias,
-                                                          int E, int topk, float scale, int* __restrict__ idx,
-                                                          float* __restrict__ wout) {
+// Selection (one CTA per activation row, one warp per 32 experts, E <= 512).  Every expert
+// becomes one 64-bit key: the high word is the bias-corrected score as an order-preserving
+// unsigned integer (0 for NaN and -inf, which are never chosen), the low word is ~expert id, so a
+// larger key is the better choice and equal scores prefer the lower id.  A warp sorts its 32 keys
+// with a bitonic network over shuffles; the sorted runs then meet in a binary tree of merges that
+// each keep the best 32 of 64 keys (the larger of a run and the partner run reversed is a bitonic
+// sequence holding them; five half-cleaner steps sort it).  The first topk keys of the final run
+// are the choices in selection order.
+__device__ __forceinline__ unsigned long long route_key(float v, int e) {
+  if (!(v > -INFINITY)) return 0ull;  // NaN and -inf are never chosen
+  const uint32_t b = __float_as_uint(v == 0.f ? 0.f : v);  // -0 and +0 compare equal
+  const uint32_t o = (b & 0x80000000u) ? ~b : (b | 0x80000000u);
+  return (static_cast<unsigned long long>(o) << 32) | static_cast<uint32_t>(~e);
+}
+
+__device__ __forceinline__ unsigned long long shfl_key(unsigned long long k, int m) {
+  return __shfl_xor_sync(0xffffffffu, k, m);
+}
+
+// 32 keys over the lanes of a warp -> descending (lane 0 holds the largest)
+__device__ __forceinline__ unsigned long long warp_sort_desc(unsigned long long k, int lane) {
+#pragma unroll
+  for (int blk = 2; blk <= 32; blk <<= 1) {
+#pragma unroll
+    for (int m = blk >> 1; m > 0; m >>= 1) {
+      const unsigned long long o = shfl_key(k, m);
+      // inside a descending block the lower lane of a pair keeps the larger key
+      const bool desc = (lane & blk) == 0, lower = (lane & m) == 0;
+      k = (desc == lower) ? (o > k ? o : k) : (o < k ? o : k);
+    }
+  }
+  return k;
+}
+
+// k: a descending run over the lanes; p: lane's key of a descending partner run taken in reverse
+// order.  Returns the best 32 of both runs, descending.
+__device__ __forceinline__ unsigned long long warp_merge_best(unsigned long long k, unsigned long long p, int lane) {
+  k = p > k ? p : k;  // bitonic, holds the 32 largest keys of the union
+#pragma unroll
+  for (int m = 16; m > 0; m >>= 1) {
+    const unsigned long long o = shfl_key(k, m);
+    k = ((lane & m) == 0) ? (o > k ? o : k) : (o < k ? o : k);
+  }
+  return k;
+}
+
+__global__ void __launch_bounds__(512) router_select_kernel(const float* __restrict__ scores,
+                                                            const float* __restrict__ bias, int E, int topk,
+                                                            float scale, int* __restrict__ idx,
+                                                            float* __restrict__ wout) {
+  __shared__ unsigned long long runs[16][32];
+  __shared__ float srow[512];
   pdl_trigger();
   pdl_wait();
-  const int r = blockIdx.x, lane = threadIdx.x;
-  float val[16], sc[16];
-#pragma unroll
-  for (int i = 0; i < 16; ++i) {
-    const int e = i * 32 + lane;
-    if (e < E) {
-      sc[i] = scores[static_cast<int64_t>(r) * E + e];
-      val[i] = sc[i] + bias[e];
-    } else {
-      sc[i] = 0.f;
-      val[i] = -INFINITY;
-    }
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nw = blockDim.x >> 5;
+  const int64_t r = blockIdx.x;
+  const int e = threadIdx.x;
+  float s = 0.f;
+  unsigned long long key = 0ull;
+  if (e < E) {
+    s = scores[r * E + e];
+    key = route_key(s + bias[e], e);
   }
-  int my_idx = -1;
-  float my_sc = 0.f, total = 0.f;
-  for (int j = 0; j < topk; ++j) {
-    float bv = -INFINITY;
-    int bi = 0x7fffffff;
-    float bs = 0.f;
-#pragma unroll
-    for (int i = 0; i < 16; ++i)  // ascending expert id per lane: strict > keeps the lowest id on ties
-      if (val[i] > bv) { bv = val[i]; bi = i * 32 + lane; bs = sc[i]; }
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) {
-      const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
-      const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
-      const float os = __shfl_xor_sync(0xffffffffu, bs, o);
-      if (ov > bv || (ov == bv && oi < bi)) { bv = ov; bi = oi; bs = os; }
-    }
-    const bool found = bv > -INFINITY;
-    if (found && (bi & 31) == lane) {
-#pragma unroll
-      for (int i = 0; i < 16; ++i)
-        if (i == (bi >> 5)) val[i] = -INFINITY;
-    }
-    const float s = found ? bs : 0.f;
-    if (lane == j) { my_idx = found ? bi : -1; my_sc = s; }
-    total += s;
+  srow[e] = s;
+  key = warp_sort_desc(key, lane);
+  for (int span = 1; span < nw; span <<= 1) {
+    runs[warp][lane] = key;
+    __syncthreads();
+    if ((warp & (2 * span - 1)) == 0 && warp + span < nw) key = warp_merge_best(key, runs[warp + span][31 - lane], lane);
+    __syncthreads();
   }
-  const float denom = total + 1e-20f;
+  if (nw == 1) __syncwarp();  // srow written by this warp only
+  if (warp != 0) return;
+  const bool chosen = lane < topk && (key >> 32) != 0ull;
+  const int ce = chosen ? static_cast<int>(~static_cast<uint32_t>(key)) : -1;
+  const float cs = chosen ? srow[ce] : 0.f;
+  // the weights' denominator adds the chosen scores in selection order, as the op defines it
+  float total = 0.f;
+  for (int j = 0; j < topk; ++j) total += __shfl_sync(0xffffffffu, cs, j);
   if (lane < topk) {
-    idx[r * topk + lane] = my_idx;
-    wout[r * topk + lane] = my_sc / denom * scale;
+    idx[r * topk + lane] = ce;
+    wout[r * topk + lane] = cs / (total + 1e-20f) * scale;
   }
 }
 
@@ -661,7 +694,8 @@ cudaError_t launch_moe_route(const bf16* x, const bf16* gate_w, const float* bia
   if (e != cudaSuccess) return e;
   LaunchCfg c2 = cfg;
   c2.pdl = true;  // same op: the selection waits for the logits with griddepcontrol.wait
-  return launch_kernel(router_topk_kernel, dim3(R), dim3(32), 0, c2, scores, bias, E, topk, scale, idx, w);
+  const unsigned threads = static_cast<unsigned>(32 * ((E + 31) / 32));
+  return launch_kernel(router_select_kernel, dim3(R), dim3(threads), 0, c2, scores, bias, E, topk, scale, idx, w);
 }
 
 cudaError_t launch_moe_decode_simt(const bf16* z, const int* idx, const float* w, const uint8_t* fc1_w, const bf16* fc1_s,

@@ -63,6 +63,30 @@ def test_route_ties_go_to_lower_index():
     assert torch.allclose(w.cpu(), torch.full((2, 4), 0.25))
 
 
+@pytest.mark.parametrize("E,topk", [(1, 1), (5, 8), (31, 8), (32, 32), (33, 9), (70, 4), (304, 8), (497, 32),
+                                    (512, 32), (512, 1)])
+def test_route_selection_bit_exact(E, topk):
+    # x = 0 makes every logit 0 and every score exactly 0.5, so the bias alone orders the experts
+    # and the selection can be compared bit for bit: values drawn from a small set (exact ties,
+    # +0 / -0, +-inf, NaN) plus random ones exercise the tie rule, the never-chosen values and the
+    # selection order; the weights (0.5 / sum in selection order * scale) must match exactly too
+    g = torch.Generator().manual_seed(E * 37 + topk)
+    pool = torch.tensor([0.5, 0.25, -0.0, 0.0, 1.5, -2.0, float("inf"), float("-inf"), float("nan"), 0.125])
+    for trial in range(4):
+        b = pool[torch.randint(0, len(pool), (E,), generator=g)]
+        rnd = torch.rand(E, generator=g) < 0.3
+        b[rnd] = torch.randn(int(rnd.sum()), generator=g)
+        if trial == 3:
+            b[:] = float("-inf")  # nothing can be chosen
+        x = torch.zeros(3, 256, dtype=torch.bfloat16)
+        gw = torch.randn(E, 256, generator=g).to(torch.bfloat16)
+        idx, w, s = ops.MoeRoute(x.to(DEV), gw.to(DEV), b.to(DEV), topk, 3.0)
+        oi, ow, osc = O.moe_route(x, gw, b, topk, 3.0)
+        assert torch.equal(s.cpu(), osc)
+        assert torch.equal(idx.cpu(), oi), (trial, idx.cpu()[0].tolist(), oi[0].tolist())
+        assert torch.equal(w.cpu(), ow)
+
+
 def test_route_topk_above_expert_count():
     d = W.moe_route(R=1, E=5, K=256, seed=1)
     idx, w, s = ops.MoeRoute(d["x"], d["gate_w"], d["bias"], 8, 1.0)
