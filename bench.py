@@ -396,61 +396,111 @@ def max_over_ranks(v, world):
     return float(t.item())
 
 
-def sharded_moe_measure(world, rank, device, iq2=0, E=304, I=2304, R=8, topk=8, iters=30, warmup=5):
-    """Expert-sharded MoeVerify step, two ways: the fused op (shard kernels, then a finalize
-    kernel that sums the ranks' partials through NVLink peer memory) and the NCCL path (shard
-    kernels, fp32 NCCL all-reduce, bf16 cast); plus the shard kernels alone.
+def _gather_equal(t, world):
+    """True when every rank holds the same bits in ``t``."""
+    if world == 1:
+        return True
+    import torch.distributed as dist
+    parts = [torch.empty_like(t) for _ in range(world)]
+    dist.all_gather(parts, t.contiguous())
+    return all(torch.equal(parts[0], q) for q in parts[1:])
 
-    Every rank routes the same seeded inputs and holds only its own experts' weights (rotated
-    copies larger than 3x L2).  The steps are replayed from a CUDA graph; times are CUDA events
-    on the compute stream, max over ranks."""
+
+def _all_ok(ok, world):
+    if world == 1:
+        return bool(ok)
+    import torch.distributed as dist
+    f = torch.tensor([1 if ok else 0], dtype=torch.int32, device="cuda")
+    dist.all_reduce(f, op=dist.ReduceOp.MIN)
+    return bool(f.item())
+
+
+def sharded_measure(world, rank, device, op="MoeVerify", iq2=0, E=304, I=2304, R=8, topk=8, iters=30, warmup=5,
+                    us_1gpu=None):
+    """Expert-sharded MoeVerify / MoeDecode step: every rank routes the same seeded inputs, holds
+    only its own experts' weights and computes its fp32 partial; the partials are summed either
+    by an NCCL all-reduce followed by the bf16 cast (the default path) or, where that path is
+    built and tested (MoeVerify at 2 GPUs), inside the op's last kernel through NVLink peer memory.
+
+    Parity first: on one seeded full expert set, every rank compares its bf16 output of each path
+    with the single-GPU op run on the full weights (within 1e-3 + 1e-2 * |ref|) and all ranks
+    must hold identical bits.  Then timing: CUDA-graph replays over rotated local weight copies
+    (larger than 3x L2), CUDA events on the compute stream, max over ranks."""
     import torch.distributed as dist
 
     from nemotron_ops_b200 import ops
     from nemotron_ops_b200 import workloads as W
-    from nemotron_ops_b200.sharded import PeerReducer, ShardedMoeVerify
+    from nemotron_ops_b200.sharded import PeerReducer, expert_range
 
+    verify = op == "MoeVerify"
     r = W.moe_route(R=R, E=E, K=4096, seed=0, device=device)
     idx, w, _ = ops.MoeRoute(r["x"], r["gate_w"], r["bias"], topk, 5.0)
     z = W.moe_latent(R=R, device=device)
-    moe = ShardedMoeVerify(E, topk, iq2)
-    e0, e1 = moe.e_begin, moe.e_end
-    one = W.moe_experts(E=e1 - e0, I=I, iq2=iq2, seed=10 + rank, device=device)
-    per_copy = sum(t.numel() * t.element_size() for t in one.values())
-    copies = max(2, int((3 * L2_BYTES) // max(1, per_copy)) + 1)
-    sets = [one] + [W.moe_experts(E=e1 - e0, I=I, iq2=iq2, seed=20 + rank + 8 * c, device=device)
-                    for c in range(copies - 1)]
-    weights = [[d[k] for k in ("fc1_w", "fc1_s", "fc2_w", "fc2_s")] for d in sets]
-    ids = idx.reshape(-1).tolist()
-    local_uniq = len({e for e in ids if e0 <= e < e1})
-    per_expert = per_copy // (e1 - e0)
-
+    e0, e1 = expert_range(E, rank, world)
+    keys = ("fc1_w", "fc1_s", "fc2_w", "fc2_s")
     P = R * topk
     out_p = torch.empty(R, 1024, dtype=torch.float32, device=device)
     out = torch.empty(R, 1024, dtype=torch.bfloat16, device=device)
     scratch = (torch.empty(P, I, dtype=torch.bfloat16, device=device),
                torch.empty(P, 1024, dtype=torch.float32, device=device),
                torch.empty(1 + P + 8 * P, dtype=torch.int32, device=device))
+    # the fused peer-memory reduction runs where its test runs: MoeVerify at 2 GPUs
+    reducer = PeerReducer(max_rows=R, device=device) if (verify and world == 2) else None
 
-    # the fused peer-memory reduction is timed beside the NCCL path at 2 GPUs, where its test runs
-    reducer = PeerReducer(max_rows=R, device=device) if world == 2 else None
-
-    def run(i, mode):
+    def run(wts, mode):
         if mode == "peer":
-            ops.moe_verify_shard_allreduce(z, idx, w, *weights[i % copies], topk=topk, iq2=iq2, e_begin=e0,
-                                           e_end=e1, reducer=reducer, num_experts=E, out=out, outputs=scratch)
+            ops.moe_verify_shard_allreduce(z, idx, w, *wts, topk=topk, iq2=iq2, e_begin=e0, e_end=e1,
+                                           reducer=reducer, num_experts=E, out=out, outputs=scratch)
             return
-        ops.moe_verify_shard(z, idx, w, *weights[i % copies], topk=topk, iq2=iq2, e_begin=e0, e_end=e1,
-                             num_experts=E, out_partial=out_p, outputs=scratch)
+        if verify:
+            ops.moe_verify_shard(z, idx, w, *wts, topk=topk, iq2=iq2, e_begin=e0, e_end=e1, num_experts=E,
+                                 out_partial=out_p, outputs=scratch)
+        else:
+            ops.moe_decode_shard(z, idx, w, *wts, topk=topk, e_begin=e0, e_end=e1, num_experts=E,
+                                 out_partial=out_p, outputs=scratch[:2])
         if mode == "nccl":
             dist.all_reduce(out_p, op=dist.ReduceOp.SUM)
         ops.f32_to_bf16(out_p, out=out)
 
+    modes = ["nccl", "local"] + (["peer"] if reducer is not None else [])
+
+    # ---- parity against the single-GPU op on the full weights
+    full = W.moe_experts(E=E, I=I, iq2=iq2, seed=99, device=device)
+    fa = [z, idx, w] + [full[k] for k in keys]
+    ref = (ops.MoeVerify(*fa, topk=topk, iq2=iq2)[0] if verify else ops.MoeDecode(*fa, topk=topk)[0]).clone()
+    loc = [full[k][e0:e1].contiguous() for k in keys]
+    parity = {}
+    for mode in ("nccl", "peer"):
+        if mode not in modes:
+            parity[mode] = None
+            continue
+        run(loc, mode)
+        torch.cuda.synchronize()
+        d = (out.float() - ref.float()).abs()
+        ok = bool((d <= 1e-3 + 1e-2 * ref.float().abs()).all()) and ops.device_status() == 0
+        same = _gather_equal(out, world)
+        ok = _all_ok(ok, world)
+        parity[mode] = {"ok": bool(ok and same), "ranks_identical": bool(same),
+                        "max_abs_err": round(max_over_ranks(float(d.max()), world), 6),
+                        "bit_equal_1gpu": _all_ok(bool(torch.equal(out, ref)), world)}
+    del full, fa, loc
+    torch.cuda.empty_cache()
+
+    # ---- timing over rotated local weight copies
+    one = W.moe_experts(E=e1 - e0, I=I, iq2=iq2, seed=10 + rank, device=device)
+    per_copy = sum(t.numel() * t.element_size() for t in one.values())
+    copies = max(2, int((3 * L2_BYTES) // max(1, per_copy)) + 1)
+    sets = [one] + [W.moe_experts(E=e1 - e0, I=I, iq2=iq2, seed=20 + rank + 8 * c, device=device)
+                    for c in range(copies - 1)]
+    weights = [[d[k] for k in keys] for d in sets]
+    ids = idx.reshape(-1).tolist()
+    local_uniq = len({e for e in ids if e0 <= e < e1})
+    local_pairs = sum(1 for e in ids if e0 <= e < e1)
+    per_expert = per_copy // (e1 - e0)
+
     def timed(mode):
-        # CUDA graph of `iters` steps (shard kernels, NCCL all-reduce, cast) over rotated weights,
-        # like the single-GPU legs; every rank captures and replays the same collectives
         for i in range(warmup):
-            run(i, mode)
+            run(weights[i % copies], mode)
         torch.cuda.synchronize()
         barrier(world)
         side = torch.cuda.Stream()
@@ -459,7 +509,7 @@ def sharded_moe_measure(world, rank, device, iq2=0, E=304, I=2304, R=8, topk=8, 
         with torch.cuda.stream(side):
             with torch.cuda.graph(g):
                 for i in range(iters):
-                    run(i, mode)
+                    run(weights[i % copies], mode)
         torch.cuda.current_stream().wait_stream(side)
         g.replay()
         torch.cuda.synchronize()
@@ -474,17 +524,25 @@ def sharded_moe_measure(world, rank, device, iq2=0, E=304, I=2304, R=8, topk=8, 
         barrier(world)
         return us
 
-    us_nccl = timed("nccl")
-    us_compute = timed("local")
-    us_total = timed("peer") if reducer is not None else us_nccl
-    uniq_all = max_over_ranks(float(local_uniq), world)
-    return {"workload": f"sharded MoeVerify {'iq2=2' if iq2 else 'int4'} R={R} E={E} k={topk} I={I} over {world} GPUs",
-            "us_per_call": round(us_nccl, 2), "path": "shard kernels, NCCL all-reduce, cast (the default)",
-            "us_shard_compute": round(us_compute, 2), "us_allreduce_and_cast": round(us_nccl - us_compute, 2),
-            "us_per_call_fused_peer_reduction": round(us_total, 2),
-            "us_exchange_fused_peer_reduction": round(us_total - us_compute, 2),
-            "max_local_unique_experts": int(uniq_all), "bytes_max_rank": int(uniq_all * per_expert),
-            "experts_per_rank": e1 - e0}
+    us = {m: timed(m) for m in modes}
+    uniq_max = int(max_over_ranks(float(local_uniq), world))
+    uniq_sum = float(local_uniq)
+    if world > 1:
+        t = torch.tensor([uniq_sum], dtype=torch.float64, device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.SUM)
+        uniq_sum = float(t.item())
+    mean_u = uniq_sum / world
+    res = {"us": round(us["nccl"], 2), "path": "shard kernels + NCCL fp32 all-reduce + cast",
+           "us_compute": round(us["local"], 2), "us_exchange": round(us["nccl"] - us["local"], 2),
+           "us_peer": round(us["peer"], 2) if "peer" in us else None,
+           "us_exchange_peer": round(us["peer"] - us["local"], 2) if "peer" in us else None,
+           "parity": parity, "U_max": uniq_max, "U_imbalance": round(uniq_max / max(mean_u, 1e-9), 2),
+           "bytes_max_rank": int(uniq_max * per_expert), "experts_per_rank": e1 - e0,
+           "local_pairs_rank0": local_pairs if rank == 0 else None}
+    if us_1gpu:
+        res["us_1gpu"] = round(us_1gpu, 2)
+        res["speedup_vs_1gpu"] = round(us_1gpu / us["nccl"], 3)
+    return res
 
 
 def capture(calls, reps):
@@ -604,6 +662,7 @@ def main():
     ap.add_argument("--workload", default="nvfp4_r1", choices=sorted(WORKLOADS))
     ap.add_argument("--no-extra", action="store_true", help="skip the other configs")
     ap.add_argument("--no-cpu", action="store_true", help="skip the cpu_baseline leg")
+    ap.add_argument("--extra", default="", help="comma-separated subset of the other configs to measure (default: all)")
     ap.add_argument("--pdl", type=int, default=1, choices=[0, 1, 2],
                     help="0: plain launches; 1: programmatic dependent launch (the library default); "
                          "2: PDL with early weight streaming")
@@ -638,29 +697,31 @@ def main():
 
     extra = {}
     if not args.no_extra:
-        for name in WORKLOADS:
-            if name == args.workload:
+        subset = [n for n in args.extra.split(",") if n] or list(WORKLOADS)
+        for name in subset:
+            if name == args.workload or name not in WORKLOADS:
                 continue
             try:
                 tmp = WORKLOADS[name][1](device, 1)
                 cp = max(3, int((3 * L2_BYTES) // tmp["bytes"]) + 1)
                 del tmp
                 r = measure(name, device, 5, 3, world, cp)
-                extra[name] = {"workload": r["desc"], "us_per_call": round(r["us_call"], 3),
-                               "gb_s": round(r["gbs"], 1), "frac_of_hbm_peak": round(r["gbs"] / hbm, 4),
-                               "bytes_per_call": r["wl"]["bytes"]}
+                extra[name] = {"us": round(r["us_call"], 2), "frac": round(r["gbs"] / hbm, 3)}
                 if "unique_experts" in r["wl"]:
-                    extra[name]["unique_experts"] = r["wl"]["unique_experts"]
+                    extra[name]["U"] = r["wl"]["unique_experts"]
                 del r
             except Exception as e:  # report, never hide
                 extra[name] = {"error": str(e)[:200]}
             torch.cuda.empty_cache()
 
     if world > 1 and not args.no_extra:  # the one path with a real exchange step
-        for q in (0, 2):
-            name = "moe_verify_sharded" + ("_iq2n" if q else "")
+        legs = (("moe_verify_sharded", "MoeVerify", 0, 8, "moe_verify_r8"),
+                ("moe_verify_iq2n_sharded", "MoeVerify", 2, 8, "moe_verify_iq2n_r8"),
+                ("moe_decode_sharded", "MoeDecode", 0, 1, "moe_decode_r1"))
+        for name, op, q, rows, one_gpu in legs:
             try:
-                extra[name] = sharded_moe_measure(world, rank, device, iq2=q)
+                extra[name] = sharded_measure(world, rank, device, op=op, iq2=q, R=rows,
+                                              us_1gpu=(extra.get(one_gpu) or {}).get("us"))
             except Exception as e:  # report, never hide
                 extra[name] = {"error": str(e)[:200]}
             torch.cuda.empty_cache()

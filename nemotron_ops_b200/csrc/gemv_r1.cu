@@ -1,0 +1,186 @@
+// Nvfp4Gemv at R = 1: a streaming SIMT GEMV (the reference's R = 1 kernel is Nvfp4GemvKernel,
+// src/bolt_ops.cu:663-736).  Arithmetic: each e2m1 weight times fp16(x * 2^-6) is formed exactly
+// and summed in fp32 (mixed-precision fma.rn.f32.f16) over its 16-weight scale block, the block
+// sum is multiplied by its e4m3 scale and accumulated in fp32; y = bf16(sum * g * 2^6).  (The
+// reference sums the block in fp16; fp32 keeps outputs that cancel within the elementwise bound.)
+//
+// B200 design
+//  * one CTA per SM, 16 warps; a CTA owns N / grid consecutive rows and a warp the rows w,
+//    w + 16, ... of it, two at a time.  A warp reads a row as 512 contiguous bytes per load
+//    instruction (16 bytes per lane, 1024 k), so every request is whole 128-byte lines, and it
+//    issues the loads of both rows over the whole of K (16 KB per warp, 128 KB per CTA) before
+//    the first use: the full weight stream of the SM is in flight at once, with no shared-memory
+//    staging, barriers or producer warp;
+//  * a lane decodes its 32 e2m1 per row and chunk with one cvt.rn.f16x2.e2m1x2 per byte and runs
+//    two fp32 chains per scale block; the activations sit in shared memory as fp16 * 2^-6, laid
+//    out so that a warp's 16-byte reads are contiguous (conflict-free); a row's scales are read
+//    as one 16-byte load per lane and passed through a per-warp shared-memory slot;
+//  * programmatic dependent launch: weights and scales are read after griddepcontrol.wait (an
+//    earlier kernel may write them); before it the CTA only pulls its rows into L2, which stays
+//    coherent with such writes.  With early weights the loads themselves go before the wait.
+#include "mma_decode.cuh"
+
+namespace bolt {
+
+namespace {
+
+constexpr int kR1Warps = 16;
+constexpr int kR1Threads = kR1Warps * 32;
+constexpr int kR1MaxChunks = 8;  // 1024-k chunks per row (K <= 8192)
+
+struct R1Params {
+  const bf16* x;
+  const uint8_t* w;
+  const uint8_t* sc;
+  const float* gscale;
+  bf16* y;
+  int64_t N;
+  int K;
+  int early_weights;
+};
+
+__device__ __forceinline__ uint4 ldg_stream(const void* p) {
+  uint4 v;
+  asm volatile("ld.global.nc.L1::no_allocate.L2::256B.v4.u32 {%0, %1, %2, %3}, [%4];"
+               : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+               : "l"(p));
+  return v;
+}
+
+// a += lo(w) * lo(x), b += hi(w) * hi(x): fp16 products (exact here) added in fp32
+__device__ __forceinline__ void fma2_f16_f32(uint32_t w, uint32_t x, float& a, float& b) {
+  asm("{\n .reg .f16 wl, wh, xl, xh;\n mov.b32 {wl, wh}, %2;\n mov.b32 {xl, xh}, %3;\n"
+      " fma.rn.f32.f16 %0, wl, xl, %0;\n fma.rn.f32.f16 %1, wh, xh, %1;\n}\n"
+      : "+f"(a), "+f"(b)
+      : "r"(w), "r"(x));
+}
+
+// sum of 16 e2m1 weights (8 bytes) times 16 fp16 activations (8 pairs), in fp32
+__device__ __forceinline__ float block_dot(uint32_t w0, uint32_t w1, const uint32_t* xp) {
+  uint32_t d[8];
+  RawRow r;
+  r.w = make_uint4(w0, w1, 0u, 0u);
+  decode_row_raw<kFmtFp4>(r, d);
+  float a = 0.f, b = 0.f;
+#pragma unroll
+  for (int j = 0; j < 8; ++j) fma2_f16_f32(d[j], xp[j], a, b);
+  return a + b;
+}
+
+template <int KC>
+__global__ void __launch_bounds__(kR1Threads, 1) gemv_nvfp4_r1_kernel(const R1Params p) {
+  extern __shared__ __align__(16) uint8_t smem[];  // x as fp16 * 2^-6: [chunk][part 0..3][lane][16 B]
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int K = p.K;
+  const int64_t rb = K / 2, srb = K / 16;
+  const int64_t r0 = static_cast<int64_t>(blockIdx.x) * p.N / gridDim.x;
+  const int64_t r1 = static_cast<int64_t>(blockIdx.x + 1) * p.N / gridDim.x;
+  pdl_trigger();
+
+  uint4 wv[2][KC];
+  uint4 sv[2];  // bytes 16 * lane .. + 15 of each row's e4m3 scales (K / 16 <= 512 bytes)
+  auto load_rows = [&](int64_t ra) {  // rows ra and ra + 16 (if inside the CTA's range)
+#pragma unroll
+    for (int q = 0; q < 2; ++q) {
+      const int64_t r = ra + 16 * q;
+      const bool ok = r < r1;
+      const uint8_t* wr = p.w + r * rb + 16 * lane;
+#pragma unroll
+      for (int i = 0; i < KC; ++i) wv[q][i] = ok ? ldg_stream(wr + 512 * i) : make_uint4(0u, 0u, 0u, 0u);
+      sv[q] = (ok && 16 * lane < srb) ? ldg_stream(p.sc + r * srb + 16 * lane) : make_uint4(0u, 0u, 0u, 0u);
+    }
+  };
+  // per warp: two rows of scales, 2 x 512 bytes, after the activations
+  uint8_t* ssl = smem + static_cast<size_t>(K) * 2 + warp * 1024;
+
+  int64_t ra = r0 + warp;
+  if (p.early_weights) {
+    load_rows(ra);
+  } else if (tid == 0) {  // the CTA's rows are contiguous: pull them into L2 during the previous kernel
+    prefetch_span_l2(p.w + r0 * rb, static_cast<uint64_t>(r1 - r0) * rb);
+    prefetch_span_l2(p.sc + r0 * srb, static_cast<uint64_t>(r1 - r0) * srb);
+  }
+  pdl_wait();
+  if (!p.early_weights) load_rows(ra);
+
+  // activations -> fp16 * 2^-6; input piece q (8 k) goes to chunk q / 128, lane (q % 128) / 4, part q % 4
+  for (int q = tid; q < K / 8; q += kR1Threads) {
+    const uint4 v = __ldcg(reinterpret_cast<const uint4*>(p.x) + q);
+    const int i = q >> 7, l = (q & 127) >> 2, part = q & 3;
+    *reinterpret_cast<uint4*>(smem + ((i * 4 + part) * 32 + l) * 16) = x_piece_to_frag<kFmtFp4>(v);
+  }
+  const float gsv = __ldcg(p.gscale) * 64.f;
+  __syncthreads();
+
+  for (; ra < r1; ra += 32) {
+    float acc[2] = {0.f, 0.f};
+    __syncwarp();  // the previous pair's scale reads are done
+    if (16 * lane < srb) {
+      *reinterpret_cast<uint4*>(ssl + 16 * lane) = sv[0];
+      *reinterpret_cast<uint4*>(ssl + 512 + 16 * lane) = sv[1];
+    }
+    __syncwarp();
+#pragma unroll
+    for (int i = 0; i < KC; ++i) {
+      uint32_t xf[16];
+#pragma unroll
+      for (int part = 0; part < 4; ++part) {
+        const uint4 v = lds128(smem + ((i * 4 + part) * 32 + lane) * 16);
+        xf[4 * part] = v.x;
+        xf[4 * part + 1] = v.y;
+        xf[4 * part + 2] = v.z;
+        xf[4 * part + 3] = v.w;
+      }
+#pragma unroll
+      for (int q = 0; q < 2; ++q) {
+        const float b0 = block_dot(wv[q][i].x, wv[q][i].y, xf);      // block 64 i + 2 lane
+        const float b1 = block_dot(wv[q][i].z, wv[q][i].w, xf + 8);  // and the next one
+        const uint32_t s8 = *reinterpret_cast<const uint16_t*>(ssl + 512 * q + 64 * i + 2 * lane);
+        uint32_t s2;
+        asm("{\n .reg .b16 t16;\n cvt.u16.u32 t16, %1;\n cvt.rn.f16x2.e4m3x2 %0, t16;\n}\n" : "=r"(s2) : "r"(s8));
+        const float2 sc = __half22float2(bits_h2(s2));
+        acc[q] = fmaf(b0, sc.x, acc[q]);
+        acc[q] = fmaf(b1, sc.y, acc[q]);
+      }
+    }
+    if (ra + 32 < r1) load_rows(ra + 32);  // the next pair of rows of this warp, while it reduces
+#pragma unroll
+    for (int q = 0; q < 2; ++q) {
+      const float a = warp_sum(acc[q]);
+      if (lane == 0 && ra + 16 * q < r1) p.y[ra + 16 * q] = __float2bfloat16(a * gsv);
+    }
+  }
+}
+
+template <int KC>
+cudaError_t launch_r1(const R1Params& p, int grid, const LaunchCfg& cfg) {
+  const size_t smem = static_cast<size_t>(p.K) * 2 + kR1Warps * 1024;
+  auto kern = gemv_nvfp4_r1_kernel<KC>;
+  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
+  if (e != cudaSuccess) return e;
+  return launch_kernel(kern, dim3(grid), dim3(kR1Threads), smem, cfg, p);
+}
+
+}  // namespace
+
+cudaError_t launch_gemv_r1(int fmt, const bf16* x, const uint8_t* w, const void* sc, const float* gscale, int64_t N,
+                           int K, bf16* y, const LaunchCfg& cfg) {
+  if (fmt != kFmtFp4 || N < 1 || K < 1024 || K % 1024 || K / 1024 > kR1MaxChunks) return cudaErrorNotSupported;
+  if ((reinterpret_cast<uintptr_t>(w) & 15) || (reinterpret_cast<uintptr_t>(sc) & 15) ||
+      (reinterpret_cast<uintptr_t>(x) & 15))
+    return cudaErrorNotSupported;
+  R1Params p{x, w, static_cast<const uint8_t*>(sc), gscale, y, N, K, cfg.early_weights ? 1 : 0};
+  const int grid = static_cast<int>(std::min<int64_t>(cfg.sms, (N + 15) / 16));
+  switch (K / 1024) {
+    case 1: return launch_r1<1>(p, grid, cfg);
+    case 2: return launch_r1<2>(p, grid, cfg);
+    case 3: return launch_r1<3>(p, grid, cfg);
+    case 4: return launch_r1<4>(p, grid, cfg);
+    case 5: return launch_r1<5>(p, grid, cfg);
+    case 6: return launch_r1<6>(p, grid, cfg);
+    case 7: return launch_r1<7>(p, grid, cfg);
+    default: return launch_r1<8>(p, grid, cfg);
+  }
+}
+
+}  // namespace bolt

@@ -55,7 +55,7 @@ bool row_tile_map(CUtensorMap* out, const void* base, int64_t rows, int64_t row_
   static std::unordered_map<Key, CUtensorMap, KeyHash> cache;
   if ((piece_bytes != 128 && piece_bytes != 64 && piece_bytes != 16) || row_bytes % piece_bytes != 0 || pieces < 1 ||
       pieces > 256 ||
-      rows < 1 || box_rows < 8 || box_rows > 256 || box_rows % 8 || (reinterpret_cast<uintptr_t>(base) & 15))
+      rows < 1 || box_rows < 1 || box_rows > 256 || (reinterpret_cast<uintptr_t>(base) & 15))
     return false;
   int dev = 0;
   cudaGetDevice(&dev);

@@ -24,13 +24,19 @@ namespace bolt {
 //
 // Encodes (or returns the cached) map of `base` viewed as above with a box of
 // (piece_bytes, box_rows, pieces); piece_bytes is 128 or 64 (swizzled) or 16 (plain), box_rows
-// a multiple of 8 up to 256.  Returns false when the view cannot be encoded.
+// up to 256 (swz_off below assumes a multiple of 8; swz_line_off takes any count).
+// Returns false when the view cannot be encoded.
 bool row_tile_map(CUtensorMap* out, const void* base, int64_t rows, int64_t row_bytes, int pieces, int piece_bytes,
                   int box_rows);
 
 // smem byte offset of byte `b` of row `r` in a tile of `br` rows written by a row_tile_map box
 __device__ __forceinline__ uint32_t swz_off(int r, int b, int br) {
   return static_cast<uint32_t>((((b >> 7) * br + r) << 7) | ((((b >> 4) & 7) ^ (r & 7)) << 4) | (b & 15));
+}
+// as swz_off for a box of any row count: the swizzle phase is the smem line index
+__device__ __forceinline__ uint32_t swz_line_off(int r, int b, int br) {
+  const int line = (b >> 7) * br + r;
+  return static_cast<uint32_t>((line << 7) | ((((b >> 4) & 7) ^ (line & 7)) << 4) | (b & 15));
 }
 __device__ __forceinline__ uint32_t p16_off(int r, int b, int br) {
   return static_cast<uint32_t>((((b >> 4) * br + r) << 4) | (b & 15));

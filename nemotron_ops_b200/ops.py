@@ -44,8 +44,9 @@ def _check(rc):
         raise RuntimeError(last_error())
 
 
-def set_launch_options(pdl: bool = False, early_weights: bool = False, smem_budget: int = 0) -> None:
-    """Process-wide launch options (see bolt_set_launch_options in include/bolt_b200.h)."""
+def set_launch_options(pdl: bool = True, early_weights: bool = False, smem_budget: int = 0) -> None:
+    """Process-wide launch options (see bolt_set_launch_options in include/bolt_b200.h); the
+    defaults are the library's own (programmatic dependent launch on, early weights off)."""
     _check(lib().bolt_set_launch_options(int(pdl), int(early_weights), int(smem_budget)))
 
 

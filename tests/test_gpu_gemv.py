@@ -273,20 +273,32 @@ def test_unaligned_activation_mma_path_is_rejected():
         ops.Q4Gemv(x, d["B"], d["scales"])
 
 
-def test_launch_options_pdl_matches_default():
-    d = W.q4_gemv(R=1, N=4096, K=4096, seed=4)
-    y0 = ops.Q4Gemv(d["x"], d["B"], d["scales"])
+@pytest.mark.parametrize("fmt", ["q4", "nvfp4"])
+def test_launch_options_pdl_matches_default(fmt):
+    if fmt == "q4":
+        d = W.q4_gemv(R=1, N=4096, K=4096, seed=4)
+        call = lambda: ops.Q4Gemv(d["x"], d["B"], d["scales"])  # noqa: E731
+    else:
+        d = W.nvfp4_gemv(R=1, N=4096, K=8192, seed=4)
+        call = lambda: ops.Nvfp4Gemv(d["x"], d["w"], d["w_scale"], d["g"])  # noqa: E731
+    y0 = call()
     ops.set_launch_options(pdl=True, early_weights=True)
     try:
-        y1 = ops.Q4Gemv(d["x"], d["B"], d["scales"])
-        y2 = ops.Q4Gemv(d["x"], d["B"], d["scales"])
+        y1 = call()
+        y2 = call()
     finally:
         ops.set_launch_options()
-    assert torch.equal(y0, y1) and torch.equal(y1, y2)
+    ops.set_launch_options(pdl=False)
+    try:
+        y3 = call()
+    finally:
+        ops.set_launch_options()
+    assert torch.equal(y0, y1) and torch.equal(y1, y2) and torch.equal(y0, y3)
 
 
-def test_cuda_graph_capture_replay():
-    d = W.nvfp4_gemv(R=8, N=2048, K=4096, seed=8)
+@pytest.mark.parametrize("R", [1, 8])
+def test_cuda_graph_capture_replay(R):
+    d = W.nvfp4_gemv(R=R, N=2048, K=4096, seed=8)
     s = torch.cuda.Stream()
     with torch.cuda.stream(s):
         y_eager = ops.Nvfp4Gemv(d["x"], d["w"], d["w_scale"], d["g"])
