@@ -8,8 +8,8 @@
  * body of one reference op -- same inputs in the same order, same element types and
  * layouts, same attribute meaning, same shape checks and error texts -- with the tensors
  * passed as (device pointer, shape array, rank) and the outputs preallocated by the caller
- * in the shapes the reference op would allocate.  The ORT adapter (ort/bolt_ort.cc) maps
- * RegisterCustomOps onto these functions.
+ * in the shapes the reference op would allocate.  The ORT adapter (nemotron_ops_b200/ort/bolt_ort.cc,
+ * built when ORT_INCLUDE_DIR is set) registers the reference's op set over these functions.
  *
  * Conventions
  *   - Pointers are device pointers on the current CUDA device; shapes are host arrays.
@@ -208,13 +208,17 @@ BOLT_API int bolt_moe_decode_shard(const void* z, const int64_t* z_shape, int z_
  * MoeVerify without caller-provided scratch (no counterpart in the reference).  Same inputs,
  * output `out` and contract as bolt_moe_verify; its scratch outputs h, part and meta live in a
  * static 1.5 MiB device buffer inside the library (one per device), so the call allocates
- * nothing.  Limit: 8192 + R*topk*4096 + R*topk*I*2 bytes (each term rounded up to 256) must fit
- * in 1,572,864 bytes, e.g. R = 8, topk = 8 with I <= 2304; larger calls fail with a message in
- * bolt_last_error() -- use bolt_moe_verify with caller buffers for them.  The first call on a
- * device looks the buffer's address up (cudaGetSymbolAddress); make it before capturing a stream
- * into a CUDA graph.  Nothing has to start at zero: every scratch byte a call reads was written
- * by the same call.  All calls on a device share the buffer, so calls that can overlap in time
- * (different streams or threads) race: the caller must serialise them.
+ * nothing.  For callers that cannot allocate device memory at run time (a captured or
+ * pre-planned executor, a plugin host that hands out only the op's own outputs) and do not want
+ * to carry the three scratch tensors.  Limit: 8192 + R*topk*4096 + R*topk*I*2 bytes (each term
+ * rounded up to 256) must fit in 1,572,864 bytes -- R*topk = 64 fits for every I up to 8192,
+ * R*topk = 128 for I <= 4064; larger calls fail with a message in bolt_last_error() (use
+ * bolt_moe_verify with caller buffers for them).  The first call on a device looks the buffer's
+ * address up (cudaGetSymbolAddress) and keeps it for the life of the process; make that call
+ * before capturing a stream into a CUDA graph, and do not use the entry point across a
+ * cudaDeviceReset of that device.  Nothing has to start at zero: every scratch byte a call reads
+ * was written by the same call.  All calls on a device share the buffer, so calls that can
+ * overlap in time (different streams or threads) race: the caller must serialise them.
  */
 BOLT_API int bolt_moe_verify_noalloc(const void* z, const int64_t* z_shape, int z_rank, const void* idx,
                                      const void* w, const void* fc1_w, const int64_t* fc1_w_shape, int fc1_w_rank,

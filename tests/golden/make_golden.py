@@ -11,7 +11,7 @@ reference's own unmodified code.
 
 Usage (build container only; needs the reference checkout and the ``gguf`` package)::
 
-    python tests/golden/make_golden.py [--reference DIR]
+    python tests/golden/make_golden.py --reference DIR    (or BOLT_REFERENCE_DIR=DIR)
 
 Each case becomes ``tests/golden/<name>.npz`` holding the op name, attributes, inputs,
 the reference output (``ref``) and, for native IQ2_XXS GEMVs, gguf's fp32 weights
@@ -182,8 +182,11 @@ CASES = [
 
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("--reference", default=os.environ.get("BOLT_REFERENCE_DIR", "/root/reference"))
+    ap.add_argument("--reference", default=os.environ.get("BOLT_REFERENCE_DIR"),
+                    help="checkout of tianleiwu/nemotron_ops (or set BOLT_REFERENCE_DIR)")
     args = ap.parse_args()
+    if not args.reference:
+        ap.error("the reference checkout is required: pass --reference DIR or set BOLT_REFERENCE_DIR")
     torch.set_num_threads(min(8, os.cpu_count() or 1))
     mod = load_reference_tests(args.reference)
     rec = Recorder(mod)
