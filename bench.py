@@ -653,12 +653,135 @@ def run_reference(args, world, rank):
     print(json.dumps(line), flush=True)
 
 
+def _ref_gpu_workload(name, device, copies):
+    """The reference's own kernels (its src/bolt_ops.cu recompiled for sm_100a, oracle/_ref/libbolt_ref.so)
+    on one of the configs, called through ONNX Runtime's custom-op interface (the stand-in session
+    of oracle/ort_shim) with preallocated outputs: returns (calls, bytes per call, description)."""
+    from nemotron_ops_b200 import workloads as W
+    from oracle.ort_shim import build as shim_build
+    from oracle.ort_shim.shim import OrtShim
+
+    path = os.path.join(shim_build.OUT, "libbolt_ref.so")
+    if not os.path.exists(path):
+        raise RuntimeError("oracle/_ref/libbolt_ref.so is absent (built where the reference checkout exists)")
+    shim = OrtShim(os.path.join(shim_build.OUT, "libort_shim_host.so"))
+    lib = shim.load(path)
+    bf, f32, i32 = torch.bfloat16, torch.float32, torch.int32
+    desc, _ = WORKLOADS[name]
+    gemv = {"nvfp4_r1": ("nvfp4", 1, 4096, 8192), "nvfp4_r8": ("nvfp4", 8, 4096, 8192), "q8_r1": ("q8", 1, 4096, 4096),
+            "q4_r1": ("q4", 1, 8192, 4096), "q4_r8": ("q4", 8, 8192, 4096), "q4iq2n_r1": ("q4n", 1, 8192, 4096),
+            "q4iq2n_r8": ("q4n", 8, 8192, 4096)}
+    if name in gemv:
+        kind, R, N, K = gemv[name]
+        sets = []
+        for c in range(copies):
+            if kind == "nvfp4":
+                d = W.nvfp4_gemv(R=R, N=N, K=K, seed=c, device=device)
+                sets.append([d["x"], d["w"], d["w_scale"], d["g"]])
+            elif kind == "q8":
+                d = W.q8_gemv(R=R, N=N, K=K, seed=c, device=device)
+                sets.append([d["x"], d["B"], d["scales"]])
+            else:
+                d = W.q4_gemv(R=R, N=N, K=K, iq2=2 if kind == "q4n" else 0, seed=c, device=device)
+                sets.append([d["x"], d["B"], d["scales"]])
+        op = {"nvfp4": "Nvfp4Gemv", "q8": "Q8Gemv"}.get(kind, "Q4Gemv")
+        kern = shim.kernel(lib, op, **({"iq2": 2} if kind == "q4n" else {}))
+        y = torch.empty(R, N, dtype=bf, device=device)
+        nbytes = sum(t.numel() * t.element_size() for t in sets[0][1:]) + sets[0][0].numel() * 2 + R * N * 2
+        calls = [(lambda s=s: kern.run(s, [y])) for s in sets]
+        return calls, nbytes, desc, kern
+    if name.startswith("moe_route"):
+        R = 8 if name.endswith("r8") else 1
+        r = W.moe_route(R=R, E=304, K=4096, seed=0, device=device)
+        gates = [(torch.randn(304, 4096, generator=torch.Generator(device=device).manual_seed(20 + c), device=device)
+                  * 0.02).to(bf) for c in range(copies)]
+        kern = shim.kernel(lib, "MoeRoute", topk=8, scale=5.0)
+        outs = [torch.empty(R, 8, dtype=i32, device=device), torch.empty(R, 8, dtype=f32, device=device),
+                torch.empty(R, 304, dtype=f32, device=device)]
+        nbytes = 304 * 4096 * 2 + 304 * 4 + R * 4096 * 2 + R * 304 * 4 + R * 8 * 8
+        calls = [(lambda gw=gw: kern.run([r["x"], gw, r["bias"]], outs)) for gw in gates]
+        return calls, nbytes, desc, kern
+    moe = {"moe_decode_r1": ("MoeDecode", 1, 0), "moe_verify_r8": ("MoeVerify", 8, 0),
+           "moe_verify_iq2n_r8": ("MoeVerify", 8, 2)}
+    if name in moe:
+        op, R, iq2 = moe[name]
+        from nemotron_ops_b200 import ops
+        r = W.moe_route(R=R, E=304, K=4096, seed=0, device=device)
+        idx, w, _ = ops.MoeRoute(r["x"], r["gate_w"], r["bias"], 8, 5.0)  # the same routing as our arm
+        z = W.moe_latent(R=R, device=device)
+        sets = [W.moe_experts(E=304, I=2304, iq2=iq2, seed=10 + c, device=device) for c in range(copies)]
+        kern = shim.kernel(lib, op, **({"topk": 8, "iq2": iq2} if iq2 else {"topk": 8}))
+        P = R * 8
+        outs = [torch.empty(R, 1024, dtype=bf, device=device), torch.empty(P, 2304, dtype=bf, device=device),
+                torch.empty(P, 1024, dtype=f32, device=device)]
+        if op == "MoeVerify":
+            outs.append(torch.empty(1 + P + 8 * P, dtype=i32, device=device))
+        uniq = len(set(idx.reshape(-1).tolist()))
+        e0 = sets[0]
+        per_expert = sum(e0[k][0].numel() * e0[k].element_size() for k in ("fc1_w", "fc1_s", "fc2_w", "fc2_s"))
+        nbytes = uniq * per_expert + R * 1024 * 2 + R * 8 * 8 + R * 1024 * 2
+        calls = [(lambda d=d: kern.run([z, idx, w, d["fc1_w"], d["fc1_s"], d["fc2_w"], d["fc2_s"]], outs)) for d in sets]
+        return calls, nbytes, desc, kern
+    raise RuntimeError(f"no reference-GPU form of workload {name}")
+
+
+def run_reference_gpu(args, world, rank):
+    """The reference's kernels on this B200 (rank 0 alone; other ranks exit without work)."""
+    if rank != 0:
+        return
+    torch.cuda.set_device(0)
+    device = "cuda:0"
+    hbm, peak_kind = peaks()
+    names = [args.workload] + ([] if args.no_extra else
+                               [n for n in ("nvfp4_r8", "q8_r1", "q4_r1", "q4_r8", "q4iq2n_r1", "q4iq2n_r8",
+                                            "moe_decode_r1", "moe_verify_r8", "moe_verify_iq2n_r8", "moe_route_r8")
+                                if n != args.workload])
+    res = {}
+    for n in names:
+        try:
+            tmp = WORKLOADS[n][1](device, 1)
+            copies = max(3, int((3 * L2_BYTES) // tmp["bytes"]) + 1)
+            del tmp
+            calls, nbytes, desc, _k = _ref_gpu_workload(n, device, copies)
+            one = capture(calls, 1)
+            ms1, _ = time_graph(one, 3, 2, 1)
+            reps = max(1, int(20.0 / max(ms1 / 3, 1e-3)))
+            del one
+            g = capture(calls, reps)
+            steps = args.steps if n == args.workload else 5
+            ms, clocks = time_graph(g, steps, max(3, args.warmup), 1)
+            us = ms * 1e3 / (steps * reps * len(calls))
+            res[n] = {"us": round(us, 2), "frac": round(nbytes / (us * 1e3) / hbm, 3), "bytes": nbytes, "desc": desc,
+                      "clocks": clocks}
+            del g
+        except Exception as e:  # report, never hide
+            res[n] = {"error": str(e)[:200]}
+        torch.cuda.empty_cache()
+    head = res.get(args.workload, {})
+    gbs = head["bytes"] / (head["us"] * 1e3) if "us" in head else None
+    line = {"metric": METRIC, "value": round(gbs, 2) if gbs else None, "unit": "GB/s", "n_gpus": 1,
+            "steps": args.steps, "warmup": args.warmup, "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "f16", "data": "synthetic", "impl": "reference-gpu",
+            "us_per_call": head.get("us"),
+            "config": {"workload": head.get("desc", args.workload),
+                       "what": "the reference's own src/bolt_ops.cu kernels recompiled for sm_100a, called "
+                               "through its RegisterCustomOps / ComputeV2 (ONNX Runtime stand-in session, "
+                               "preallocated outputs) in CUDA graphs over rotated weight copies"},
+            "roofline": {"bound": "hbm", "peak": hbm, "unit": "GB/s", "peak_source": peak_kind,
+                         "frac": head.get("frac")},
+            "configs_measured": {n: {k: v for k, v in r.items() if k not in ("desc", "bytes", "clocks")}
+                                 for n, r in res.items() if n != args.workload}}
+    print(json.dumps(line), flush=True)
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=30)
     ap.add_argument("--warmup", type=int, default=5)
-    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference", "reference-gpu"],
+                    help="reference: the reference's CPU path (torch restatement); reference-gpu: the "
+                         "reference's own CUDA kernels recompiled for sm_100a, on this GPU")
     ap.add_argument("--workload", default="nvfp4_r1", choices=sorted(WORKLOADS))
     ap.add_argument("--no-extra", action="store_true", help="skip the other configs")
     ap.add_argument("--no-cpu", action="store_true", help="skip the cpu_baseline leg")
@@ -672,6 +795,9 @@ def main():
 
     if args.impl == "reference":  # rank 0 alone runs the CPU reference; other ranks exit without work
         run_reference(args, int(os.environ.get("WORLD_SIZE", "1")), int(os.environ.get("RANK", "0")))
+        return
+    if args.impl == "reference-gpu":
+        run_reference_gpu(args, int(os.environ.get("WORLD_SIZE", "1")), int(os.environ.get("RANK", "0")))
         return
     world, rank, local = dist_setup()
 

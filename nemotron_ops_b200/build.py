@@ -5,6 +5,8 @@
 Every csrc/*.cu is compiled to an object under csrc/_build/ (relocatable device code, so the
 translation units share the device status word), then nvcc links them into
 nemotron_ops_b200/libbolt_b200.so.  Objects are rebuilt when any source or header is newer.
+With ORT_INCLUDE_DIR set (ONNX Runtime's headers), ort/bolt_ort.cc is also built into
+libbolt_b200_ort.so, the library an ORT session registers (register_custom_ops_library).
 """
 from __future__ import annotations
 
@@ -75,6 +77,25 @@ def build(force: bool = False, jobs: int = 0, verbose: bool = False) -> str:
     return LIB
 
 
+def build_ort_adapter(force: bool = False) -> str:
+    """libbolt_b200_ort.so: the ONNX Runtime adapter (ort/bolt_ort.cc, exports RegisterCustomOps),
+    compiled only when ORT_INCLUDE_DIR names a directory holding onnxruntime_cxx_api.h (as the
+    reference's CMakeLists.txt requires); returns its path, or "" when the headers are absent."""
+    inc = os.environ.get("ORT_INCLUDE_DIR", "")
+    if not inc or not os.path.exists(os.path.join(inc, "onnxruntime_cxx_api.h")):
+        return ""
+    lib = build(force)
+    out = os.path.join(PKG, "libbolt_b200_ort.so")
+    src = os.path.join(PKG, "ort", "bolt_ort.cc")
+    if force or _stale(out, [src, lib, os.path.join(INCLUDE, "bolt_b200.h")]):
+        cmd = [shutil.which("g++") or "g++", "-std=c++17", "-O2", "-fPIC", "-shared", "-I", inc, "-I", INCLUDE, src,
+               "-L", PKG, "-l:libbolt_b200.so", "-Wl,-rpath,$ORIGIN", "-o", out]
+        r = subprocess.run(cmd, capture_output=True, text=True)
+        if r.returncode != 0:
+            raise RuntimeError(f"ORT adapter build failed:\n{r.stdout}\n{r.stderr}")
+    return out
+
+
 def main(argv=None):
     ap = argparse.ArgumentParser()
     ap.add_argument("--force", action="store_true")
@@ -82,6 +103,9 @@ def main(argv=None):
     ap.add_argument("-v", action="store_true")
     a = ap.parse_args(argv)
     print(build(a.force, a.j, a.v))
+    ort = build_ort_adapter(a.force)
+    if ort:
+        print(ort)
 
 
 if __name__ == "__main__":
