@@ -477,7 +477,11 @@ def sharded_measure(world, rank, device, op="MoeVerify", iq2=0, E=304, I=2304, R
         run(loc, mode)
         torch.cuda.synchronize()
         d = (out.float() - ref.float()).abs()
-        ok = bool((d <= 1e-3 + 1e-2 * ref.float().abs()).all()) and ops.device_status() == 0
+        # the op's tolerance plus 1% of the output's largest magnitude: a shard sums its pairs in its
+        # own fp32 order and the exchange adds the shards, so a row that cancels to near zero keeps
+        # the rounding of its large terms (the same bound as tests/test_gpu_sharded.py)
+        tol = 1e-3 + 1e-2 * ref.float().abs() + 1e-2 * ref.float().abs().max()
+        ok = bool((d <= tol).all()) and ops.device_status() == 0
         same = _gather_equal(out, world)
         ok = _all_ok(ok, world)
         parity[mode] = {"ok": bool(ok and same), "ranks_identical": bool(same),
