@@ -111,6 +111,14 @@ cudaError_t launch_moe_route(const bf16* x, const bf16* gate_w, const float* bia
 cudaError_t launch_moe_decode(const bf16* z, const int* idx, const float* w, const uint8_t* fc1_w, const bf16* fc1_s,
                               const uint8_t* fc2_w, const bf16* fc2_s, int R, int E, int I, int topk, int e_begin,
                               int e_end, bf16* out, bf16* h, float* part, float* out_partial, const LaunchCfg& cfg);
+// MoeDecode on the register-streaming kernels (moe_stream.cu; P <= 128, R <= 16, I % 32 == 0,
+// I <= 8192, P * (I / 32) * 68 + 512 * ceil(1024 / sms) bytes of shared memory <= 200 KB,
+// 16-byte aligned z, weights and h): cudaErrorNotSupported, with nothing launched, for shapes
+// they do not take.
+cudaError_t launch_moe_decode_stream(const bf16* z, const int* idx, const float* w, const uint8_t* fc1_w,
+                                     const bf16* fc1_s, const uint8_t* fc2_w, const bf16* fc2_s, int R, int E, int I,
+                                     int topk, int e_begin, int e_end, bf16* out, bf16* h, float* part,
+                                     float* out_partial, const LaunchCfg& cfg);
 // MoeDecode for any I % 32 == 0 (SIMT), all experts.
 cudaError_t launch_moe_decode_simt(const bf16* z, const int* idx, const float* w, const uint8_t* fc1_w,
                                    const bf16* fc1_s, const uint8_t* fc2_w, const bf16* fc2_s, int R, int E, int I,

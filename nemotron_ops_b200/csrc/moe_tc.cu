@@ -780,6 +780,11 @@ cudaError_t launch_moe_decode(const bf16* z, const int* idx, const float* w, con
                               const uint8_t* fc2_w, const bf16* fc2_s, int R, int E, int I, int topk, int e_begin,
                               int e_end, bf16* out, bf16* h, float* part, float* out_partial, const LaunchCfg& cfg) {
   const int P = R * topk;
+  {  // bulk-copy streaming kernels (moe_stream.cu) where they take the shape
+    const cudaError_t e = launch_moe_decode_stream(z, idx, w, fc1_w, fc1_s, fc2_w, fc2_s, R, E, I, topk, e_begin, e_end,
+                                               out, h, part, out_partial, cfg);
+    if (e != cudaErrorNotSupported) return e;
+  }
   cudaError_t e = launch_grouped(kFmtQ4, true, 1, false, z, nullptr, idx, fc1_w, fc1_s, h, nullptr, P, R, topk, E,
                                  e_begin, e_end, 1024, I, cfg);
   if (e != cudaSuccess) return e;
