@@ -234,6 +234,14 @@ __global__ void __launch_bounds__(kMsThreads, 1) moe_stream_fc1_kernel(const MsP
   // z, idx and w come from the previous kernels of the stream
   pdl_wait();
   pdl_trigger();
+  // the lane's 32 activations of one token (R * 32 jobs), loaded while the groups form
+  const bool zjob = tid < p.R * 32;
+  uint4 zv[4];
+  if (zjob) {
+    const uint4* zr = reinterpret_cast<const uint4*>(p.z + static_cast<int64_t>(tid >> 5) * 1024 + 32 * (tid & 31));
+#pragma unroll
+    for (int j = 0; j < 4; ++j) zv[j] = __ldcg(zr + j);
+  }
   build_groups(p, g, blockIdx.x == 0);
   const int I = p.I;
   // units (group, row j) in a flat index < U * I <= 128 * 4096; the CTA owns [u0, u1)
@@ -265,6 +273,20 @@ __global__ void __launch_bounds__(kMsThreads, 1) moe_stream_fc1_kernel(const MsP
     }
   };
   issue();
+  {  // fc2's weights of these experts into L2 (fc2 loads them from there): this CTA's share, one
+     // 128-byte line per thread and step
+    const uint32_t per_w = 1024u * (I / 2), per = per_w + 1024u * (I / 16);  // bytes per expert
+    const uint32_t tot = static_cast<uint32_t>(g.U) * per;
+    const uint32_t b0 = static_cast<uint32_t>(static_cast<uint64_t>(blockIdx.x) * tot / gridDim.x) & ~127u;
+    const uint32_t b1 = static_cast<uint32_t>(static_cast<uint64_t>(blockIdx.x + 1) * tot / gridDim.x);
+    for (uint32_t o = b0 + 128u * tid; o < b1; o += 128u * kMsThreads) {
+      const uint32_t gi = o / per, off = o - gi * per;
+      const int64_t e = g.gexp[gi];
+      const uint8_t* a = off < per_w ? p.w2 + e * per_w + off
+                                     : reinterpret_cast<const uint8_t*>(p.s2) + e * (1024 * (I / 16)) + (off - per_w);
+      asm volatile("prefetch.global.L2 [%0];" ::"l"(a));
+    }
+  }
   if (blockIdx.x == 0)  // pairs whose expert id is outside [0, E): zero h rows
     for (int q = 0; q < p.P; ++q)
       if (g.es[q] == kBadPair)
@@ -272,13 +294,10 @@ __global__ void __launch_bounds__(kMsThreads, 1) moe_stream_fc1_kernel(const MsP
   // the tokens' activations in PERM pieces [t][piece][lane] and the lanes' block sums [t][lane]
   uint4* xz = reinterpret_cast<uint4*>(dsm);
   float* xsz = reinterpret_cast<float*>(dsm + static_cast<size_t>(p.R) * 2048);
-  for (int i = tid; i < p.R * 32; i += kMsThreads) {
-    const int t = i >> 5, l = i & 31;
-    const uint4* zr = reinterpret_cast<const uint4*>(p.z + static_cast<int64_t>(t) * 1024 + 32 * l);
-    uint4 v[4], o[4];
-#pragma unroll
-    for (int j = 0; j < 4; ++j) v[j] = __ldcg(zr + j);
-    xsz[i] = perm_block(v, o);
+  if (zjob) {
+    const int t = tid >> 5, l = tid & 31;
+    uint4 o[4];
+    xsz[tid] = perm_block(zv, o);
 #pragma unroll
     for (int j = 0; j < 4; ++j) xz[(t * 4 + j) * 32 + l] = o[j];
   }
@@ -357,8 +376,10 @@ __global__ void __launch_bounds__(kMsThreads, 1) moe_stream_fc2_kernel(const MsP
   extern __shared__ __align__(16) uint8_t dsm[];
   __shared__ Groups g;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  __shared__ float ws[kMsMaxP];
   pdl_trigger();
-  // idx is an op input: this grid starts only after every fc1 CTA passed its dependency wait
+  // idx and w are op inputs: this grid starts only after every fc1 CTA passed its dependency wait
+  if (tid < p.P) ws[tid] = __ldcg(p.w + tid);
   build_groups(p, g, false);
   const int I = p.I, nchunk = I / 32, L = nchunk - 32 * F;
   const int64_t wrow = I / 2;
@@ -459,7 +480,7 @@ __global__ void __launch_bounds__(kMsThreads, 1) moe_stream_fc2_kernel(const MsP
     float acc = 0.f;
     for (int kk = 0; kk < p.topk; ++kk) {
       const int q = t * p.topk + kk;
-      if (g.es[q] >= 0) acc = fmaf(__ldcg(p.w + q), pv[r * kMsMaxP + q], acc);
+      if (g.es[q] >= 0) acc = fmaf(ws[q], pv[r * kMsMaxP + q], acc);
     }
     if (p.out) p.out[static_cast<int64_t>(t) * 1024 + n0 + r] = __float2bfloat16(acc);
     if (p.out_partial) p.out_partial[static_cast<int64_t>(t) * 1024 + n0 + r] = acc;
