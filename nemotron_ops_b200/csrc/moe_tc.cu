@@ -723,13 +723,6 @@ cudaError_t launch_grouped(int fmt, bool bc, int fc, bool verify, const bf16* x,
 
 // group kernel (moe.cu): meta of the unique experts in [e_begin, e_end)
 cudaError_t launch_moe_group(const int* idx, int P, int topk, int e_begin, int e_end, int* meta, const LaunchCfg& cfg);
-// round_part: part holds fp32 fc2 sums, rounded to bf16 (and written back) here
-cudaError_t launch_moe_finalize(float* part, int round_part, const float* w, const int* idx, int R, int topk,
-                                int e_begin, int e_end, bf16* out, float* out_partial, const LaunchCfg& cfg);
-// the same, fused with the sum over the ranks' partials through peer memory (moe.cu)
-cudaError_t launch_moe_finalize_allreduce(float* part, int round_part, const float* w, const int* idx, int R,
-                                          int topk, int e_begin, int e_end, const PeerReduce& pr, bf16* out,
-                                          const LaunchCfg& cfg);
 // tcgen05 expert layer (moe_umma.cu): whether it takes a layer, and the launch.  Its CTAs build the
 // expert list from idx themselves; fc1 zeroes part_out when given one (fc2 with split relies on
 // that to split tiles) and writes meta when given meta_out.
@@ -743,6 +736,11 @@ cudaError_t launch_moe_verify(int fmt, const bf16* z, const int* idx, const floa
                               int topk, int e_begin, int e_end, bf16* out, bf16* h, float* part, int* meta,
                               float* out_partial, const LaunchCfg& cfg, const PeerReduce* pr) {
   const int P = R * topk;
+  if (fmt == kFmtQ4) {  // register-streaming tensor-core kernels (moe_vstream.cu) where they take the shape
+    const cudaError_t e = launch_moe_verify_stream(z, idx, w, fc1_w, fc1_s, fc2_w, fc2_s, R, E, I, topk, e_begin,
+                                                   e_end, out, h, part, meta, out_partial, cfg, pr);
+    if (e != cudaErrorNotSupported) return e;
+  }
   // tcgen05 layers where they apply (int4 / native IQ2_XXS, 128-row tiles), else mma.sync.  The
   // tcgen05 layers build the expert list from idx in every CTA; the grouping kernel (which writes
   // meta, read by the mma.sync layers) runs only when a layer falls back, else fc1 writes meta.
