@@ -171,10 +171,14 @@ def _moe_workload(op_name, R, iq2=0, E=304, I=2304, topk=8, route=False):
                 O.moe_verify(*args, topk=topk, iq2=iq2, fp32=True)
             return nbytes * rows / R
 
-        kern = 3 + (2 if route else 0)  # fc1, fc2, finalize (+ router logits, top-k)
+        # launches per call: MoeDecode fc1 + fc2 (finalize fused); MoeVerify fc1, fc2, finalize
+        # (+ router logits, selection)
+        kern = (2 if op_name == "MoeDecode" else 3) + (2 if route else 0)
+        main_kernel = ("moe_stream_fc1_kernel + moe_stream_fc2_kernel" if op_name == "MoeDecode" else
+                       "moe_vstream_kernel" if iq2 == 0 else "moe_umma_kernel")
         return dict(calls=calls, bytes=nbytes, kernels=kern, h2d=R * 1024 * 2,
                     d2h=R * 1024 * 2, e2e=e2e, cpu=cpu, cpu_sample=R * topk, dtype="f32" if op_name == "MoeDecode"
-                    else "bf16", unique_experts=uniq, kernel="moe_tc_kernel")
+                    else "bf16", unique_experts=uniq, kernel=main_kernel)
     return build
 
 
@@ -788,6 +792,9 @@ def main():
                          "reference's own CUDA kernels recompiled for sm_100a, on this GPU")
     ap.add_argument("--workload", default="nvfp4_r1", choices=sorted(WORKLOADS))
     ap.add_argument("--no-extra", action="store_true", help="skip the other configs")
+    ap.add_argument("--copies", type=int, default=0,
+                    help="rotated weight copies (default: enough to exceed 3x L2); a small number is for "
+                         "profiler captures, not for bench numbers")
     ap.add_argument("--no-cpu", action="store_true", help="skip the cpu_baseline leg")
     ap.add_argument("--extra", default="", help="comma-separated subset of the other configs to measure (default: all)")
     ap.add_argument("--pdl", type=int, default=1, choices=[0, 1, 2],
@@ -810,9 +817,10 @@ def main():
     device = f"cuda:{local}"
     hbm, peak_kind = peaks()
     desc, builder = WORKLOADS[args.workload]
-    # enough distinct weight copies to exceed 3x L2
+    # enough distinct weight copies to exceed 3x L2 (--copies: fewer, for profiler captures only;
+    # the line then says so in config.cache)
     tmp = builder(device, 1)
-    copies = max(3, int((3 * L2_BYTES) // tmp["bytes"]) + 1)
+    copies = args.copies or max(3, int((3 * L2_BYTES) // tmp["bytes"]) + 1)
     del tmp
     torch.cuda.empty_cache()
     vis = os.environ.get("CUDA_VISIBLE_DEVICES")
@@ -878,8 +886,10 @@ def main():
             "us_per_call": round(m["us_call"], 3),
             "config": {"workload": desc, "calls_per_step": m["reps"] * len(wl["calls"]), "weight_copies": copies,
                        "bytes_per_call": wl["bytes"],
-                       "cache": f"inputs larger than L2: {copies} distinct weight copies ({copies_bytes / 1e6:.0f} MB) "
-                                f"rotated inside every step", "parallelism": "replicas" if world > 1 else "single",
+                       "cache": (f"inputs larger than L2: {copies} distinct weight copies ({copies_bytes / 1e6:.0f} MB) "
+                                 f"rotated inside every step") if copies_bytes > L2_BYTES else
+                                (f"profiler case: {copies} weight copies ({copies_bytes / 1e6:.0f} MB) fit in L2; not a "
+                                 f"bench number"), "parallelism": "replicas" if world > 1 else "single",
                        "launch": ("plain", "pdl", "pdl+early_weights")[args.pdl]},
             "roofline": {"bound": "hbm", "achieved": round(wl["bytes"] / (m["us_call"] * 1e3), 1), "peak": hbm,
                          "unit": "GB/s", "frac": round(wl["bytes"] / (m["us_call"] * 1e3) / hbm, 4),
