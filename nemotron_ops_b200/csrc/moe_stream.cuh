@@ -41,6 +41,7 @@ struct Groups {
   int gstart[kMsMaxP + 1]; // group g's pairs are plist[gstart[g] .. gstart[g + 1])
   int gexp[kMsMaxP];       // expert of group g
   int ptok[kMsMaxP];       // token of plist[a]
+  int pgrp[kMsMaxP];       // group of plist[a]
   int U, nl;
 };
 
@@ -144,6 +145,7 @@ __device__ void build_groups(const MsParams& p, Groups& g, bool report) {
     }
     g.plist[before + rank] = tid;
     g.ptok[before + rank] = tid / p.topk;
+    g.pgrp[before + rank] = slot;
     if (first) {
       g.gexp[slot] = e;
       g.gstart[slot] = before;

@@ -66,6 +66,8 @@ __global__ void __launch_bounds__(kMsThreads, 1) moe_vstream_kernel(const MsPara
   extern __shared__ __align__(16) uint8_t dsm[];
   __shared__ Groups g;
   __shared__ int tok_pair[kVsMaxSpan][kVsTok];  // fc2: pair of (group slot, token), -1: none
+  __shared__ int gtp[kMsMaxP][kVsTok];          // first pair of (group, token), -1: none
+  __shared__ int gdup[kMsMaxP];                 // the group has a token with two pairs
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31, gq = lane >> 2, c = lane & 3;
   const int I = p.I;
   const int K = FC == 1 ? 1024 : I, NR = FC == 1 ? I : 1024, nch = K / 128;
@@ -140,6 +142,9 @@ __global__ void __launch_bounds__(kMsThreads, 1) moe_vstream_kernel(const MsPara
       }
   };
   if (warp < nsu) issue(ua, wq[0], sq[0]);
+  // epilogue map, first pair of (group, token): cleared here, filled after the next barrier
+  for (int i = tid; i < g.U * kVsTok; i += kMsThreads) gtp[i / kVsTok][i % kVsTok] = -1;
+  if (tid < g.U) gdup[tid] = 0;
 
   // ---- bookkeeping of CTA 0: zero rows of pairs with an expert id outside [0, E); fc1 writes meta
   if (blockIdx.x == 0) {
@@ -197,11 +202,19 @@ __global__ void __launch_bounds__(kMsThreads, 1) moe_vstream_kernel(const MsPara
     }
   }
   // a zero row after the staged rows (B of tokens without a pair of the expert), then the sums
+  // two zero rows after the staged rows (B of tokens without a pair of the expert): token g reads
+  // the one whose 64-byte bank half matches its own staged row's, so the lanes stay conflict-free
   const int nbrows = FC == 1 ? p.R : span * kVsTok;
-  const uint4* bzero = bx + nbrows * rstride;
-  for (int i = tid; i < rstride; i += kMsThreads) bx[nbrows * rstride + i] = make_uint4(0u, 0u, 0u, 0u);
-  float* psum = reinterpret_cast<float*>(dsm + static_cast<size_t>(nbrows + 1) * rstride * 16);
+  const int z0 = nbrows + (nbrows & 1);  // even row index
+  for (int i = tid; i < 2 * rstride; i += kMsThreads) bx[z0 * rstride + i] = make_uint4(0u, 0u, 0u, 0u);
+  const uint4* bzero = bx + (z0 + (gq & 1)) * rstride;
+  float* psum = reinterpret_cast<float*>(dsm + static_cast<size_t>(z0 + 2) * rstride * 16);
   __syncthreads();
+  if (tid < g.nl) {  // a group's pairs ascend, so a token's pairs are adjacent
+    const int gi = g.pgrp[tid];
+    if (tid == g.gstart[gi] || g.ptok[tid - 1] != g.ptok[tid]) gtp[gi][g.ptok[tid]] = g.plist[tid];
+    else gdup[gi] = 1;
+  }
 
   // ---- sub-units: decode + MMA, sums to shared memory
   auto compute = [&](int su, const Su& u, const uint4 (&w)[kVsKG][2], const uint32_t (&s)[kVsKG][2]) {
@@ -264,16 +277,19 @@ __global__ void __launch_bounds__(kMsThreads, 1) moe_vstream_kernel(const MsPara
         for (int kg = 0; kg < spt; ++kg) v += psum[(tl * spt + kg) * 128 + pos];
         const float b = __bfloat162float(__float2bfloat16(v));
         const int row = rt * 16 + rin;
-        for (int a = g.gstart[gi]; a < g.gstart[gi + 1]; ++a) {
-          if (g.ptok[a] != t) continue;
-          const int q = g.plist[a];
+        auto put = [&](int q) {
           if constexpr (FC == 1) {
             const float rl = fmaxf(b, 0.f);
             p.h[static_cast<int64_t>(q) * I + row] = __float2bfloat16(rl * rl);
           } else {
             p.part[static_cast<int64_t>(q) * 1024 + row] = b;
           }
-        }
+        };
+        const int q = gtp[gi][t];
+        if (q >= 0) put(q);
+        if (gdup[gi])  // a token that names this expert twice: its other pairs get the same row
+          for (int a = g.gstart[gi]; a < g.gstart[gi + 1]; ++a)
+            if (g.ptok[a] == t && g.plist[a] != q) put(g.plist[a]);
       }
       rt += kStep;
       while (rt >= TE) {
@@ -300,18 +316,20 @@ cudaError_t launch_moe_verify_stream(const bf16* z, const int* idx, const float*
       (reinterpret_cast<uintptr_t>(fc2_s) & 1))
     return cudaErrorNotSupported;
   const int G = cfg.sms;
-  // shared memory: staged activation rows + the sub-unit sums of the CTA's tiles
+  // fc2: a CTA's (at most tiles2) tiles touch at most span2 groups of 64 tiles
+  const int64_t tiles2 = (static_cast<int64_t>(P) * 64 + G - 1) / G;
+  const int span2 = static_cast<int>((tiles2 + 63) / 64 + 1);
+  // shared memory: staged activation rows (+ two zero rows and a parity pad) and the sub-unit
+  // sums of the CTA's tiles
   const auto smem_for = [&](int fc) {
     const int K = fc == 1 ? 1024 : I, NR = fc == 1 ? I : 1024, nch = K / 128;
     const int spt = (nch + kVsKG - 1) / kVsKG;
     const int64_t tiles = (static_cast<int64_t>(P) * (NR / 16) + G - 1) / G;  // at most U <= P experts
-    const int rows = (fc == 1 ? R : kVsMaxSpan * kVsTok) + 1;  // + the zero row
+    const int rows = (fc == 1 ? R : span2 * kVsTok) + 3;
     return static_cast<size_t>(rows) * (nch * 16 + 4) * 16 + static_cast<size_t>(tiles) * spt * 512;
   };
   const size_t smem1 = smem_for(1), smem2 = smem_for(2);
-  // fc2: a CTA's tiles touch at most kVsMaxSpan groups
-  const int64_t tiles2 = (static_cast<int64_t>(P) * 64 + G - 1) / G;
-  if (smem1 > kVsSmemCap || smem2 > kVsSmemCap || (tiles2 + 63) / 64 + 1 > kVsMaxSpan) return cudaErrorNotSupported;
+  if (smem1 > kVsSmemCap || smem2 > kVsSmemCap || span2 > kVsMaxSpan) return cudaErrorNotSupported;
   MsParams p{z, idx, w, fc1_w, fc1_s, fc2_w, fc2_s, h, part, out, out_partial, meta, R, P, topk, E, I, e_begin, e_end,
              0};
   static std::atomic<size_t>* cur = g_vs_smem;
