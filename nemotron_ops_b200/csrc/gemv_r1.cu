@@ -18,6 +18,7 @@
 //  * programmatic dependent launch: weights and scales are read after griddepcontrol.wait (an
 //    earlier kernel may write them); before it the CTA only pulls its rows into L2, which stays
 //    coherent with such writes.  With early weights the loads themselves go before the wait.
+// The file also holds the Q4Gemv (int4) R = 1 kernel on the same streaming layout (below).
 #include "mma_decode.cuh"
 
 namespace bolt {
@@ -161,16 +162,186 @@ cudaError_t launch_r1(const R1Params& p, int grid, const LaunchCfg& cfg) {
   return launch_kernel(kern, dim3(grid), dim3(kR1Threads), smem, cfg, p);
 }
 
+// ------------------------------------------------------------------------------------------
+// Q4Gemv (int4, zero point 8) at R = 1, exact contract (the reference's R = 1 kernel is
+// QGemvKernel, src/bolt_ops.cu:1315-1392): y = bf16(sum over blocks of s * sum (q - 8) x), fp32.
+// Same streaming layout: lane l reads 16 bytes (one 32-k block) per 1024-k chunk of each row.
+// A warp takes RB rows of its CTA at a time (rows w, w + 16, ...) and shares each activation
+// chunk among them; a lane decodes bf16(128 + q) pairs (a shift and a LOP3 per two weights),
+// multiplies them by x with mixed-precision fma.rn.f32.bf16 (exact products, fp32 sums) and
+// removes 136 * (the block's sum of x); the RB row sums meet in one butterfly reduction.
+// ------------------------------------------------------------------------------------------
+__device__ __forceinline__ uint32_t ldg_u16(const void* p) {
+  unsigned short v;
+  asm volatile("ld.global.nc.L1::no_allocate.u16 %0, [%1];" : "=h"(v) : "l"(p));
+  return v;
+}
+
+// a += lo(q) * lo(x), b += hi(q) * hi(x) for bf16 pairs: exact products, fp32 sums
+__device__ __forceinline__ void fma2_bf16_f32r(uint32_t q, uint32_t x, float& a, float& b) {
+  asm("{\n .reg .b16 ql, qh, xl, xh;\n mov.b32 {ql, qh}, %2;\n mov.b32 {xl, xh}, %3;\n"
+      " fma.rn.f32.bf16 %0, ql, xl, %0;\n fma.rn.f32.bf16 %1, qh, xh, %1;\n}\n"
+      : "+f"(a), "+f"(b)
+      : "r"(q), "r"(x));
+}
+
+// sum over one 16-byte int4 block of (128 + q) * x, x as four PERM pieces (x_piece_to_frag order)
+__device__ __forceinline__ float q4_block_dot(const uint4& wq, const uint4 (&x)[4]) {
+  const uint32_t wv[4] = {wq.x, wq.y, wq.z, wq.w};
+  const uint32_t xv[16] = {x[0].x, x[0].y, x[0].z, x[0].w, x[1].x, x[1].y, x[1].z, x[1].w,
+                           x[2].x, x[2].y, x[2].z, x[2].w, x[3].x, x[3].y, x[3].z, x[3].w};
+  float a0 = 0.f, b0 = 0.f, a1 = 0.f, b1 = 0.f;
+#pragma unroll
+  for (int i = 0; i < 4; ++i)
+#pragma unroll
+    for (int s = 0; s < 4; ++s) {
+      const uint32_t d = ((wv[i] >> (4 * s)) & 0x000F000Fu) | 0x43004300u;  // bf16(128 + q), exact
+      if (s & 1) fma2_bf16_f32r(d, xv[4 * i + s], a1, b1);
+      else fma2_bf16_f32r(d, xv[4 * i + s], a0, b0);
+    }
+  return (a0 + b0) + (a1 + b1);
+}
+
+// lane l ends with the warp total of v[l >> (5 - log2 RB)] (same tree as a per-value warp sum)
+template <int RB>
+__device__ __forceinline__ float warp_sum_t(const float (&v)[RB]) {
+  const int lane = threadIdx.x & 31;
+  if constexpr (RB == 4) {
+    float w[2];
+#pragma unroll
+    for (int i = 0; i < 2; ++i) {
+      const bool up = lane & 16;
+      const float send = up ? v[i] : v[i + 2], keep = up ? v[i + 2] : v[i];
+      w[i] = keep + __shfl_xor_sync(0xffffffffu, send, 16);
+    }
+    const bool up = lane & 8;
+    const float send = up ? w[0] : w[1], keep = up ? w[1] : w[0];
+    float s = keep + __shfl_xor_sync(0xffffffffu, send, 8);
+#pragma unroll
+    for (int o = 4; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
+    return s;
+  } else {
+    const bool up = lane & 16;
+    const float send = up ? v[0] : v[1], keep = up ? v[1] : v[0];
+    float s = keep + __shfl_xor_sync(0xffffffffu, send, 16);
+#pragma unroll
+    for (int o = 8; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
+    return s;
+  }
+}
+
+template <int KC, int RB>
+__global__ void __launch_bounds__(kR1Threads, 1) gemv_q4_r1_kernel(const R1Params p) {
+  extern __shared__ __align__(16) uint8_t smem[];  // x: PERM pieces [chunk][piece][lane], block sums [chunk][lane]
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int K = p.K;
+  const int64_t rb = K / 2, srb = K / 32;  // bytes per weight row, scales per row
+  const int64_t r0 = static_cast<int64_t>(blockIdx.x) * p.N / gridDim.x;
+  const int64_t r1 = static_cast<int64_t>(blockIdx.x + 1) * p.N / gridDim.x;
+  const uint16_t* sc = reinterpret_cast<const uint16_t*>(p.sc);
+  pdl_trigger();
+
+  uint4 wv[RB][KC];
+  uint32_t sv[RB][KC];
+  auto load_rows = [&](int64_t ra) {  // rows ra, ra + 16, ... (RB of them, inside the CTA's range)
+#pragma unroll
+    for (int q = 0; q < RB; ++q) {
+      const int64_t r = ra + 16 * q;
+      if (r < r1) {
+        const uint8_t* wr = p.w + r * rb + 16 * lane;
+        const uint16_t* sr = sc + r * srb + lane;
+#pragma unroll
+        for (int i = 0; i < KC; ++i) {
+          wv[q][i] = ldg_stream(wr + 512 * i);
+          sv[q][i] = ldg_u16(sr + 32 * i);
+        }
+      }
+    }
+  };
+  int64_t ra = r0 + warp;
+  if (p.early_weights) {
+    load_rows(ra);
+  } else if (tid == 0) {  // the CTA's rows are contiguous: pull them into L2 during the previous kernel
+    prefetch_span_l2(p.w + r0 * rb, static_cast<uint64_t>(r1 - r0) * rb);
+    prefetch_span_l2(sc + r0 * srb, static_cast<uint64_t>(r1 - r0) * srb * 2);
+  }
+  pdl_wait();
+  if (!p.early_weights) load_rows(ra);
+
+  // activations: block b = 32 i + l of 32 k -> PERM pieces [i][piece][l] and the block's fp32 sum
+  uint4* xs = reinterpret_cast<uint4*>(smem);
+  float* xsum = reinterpret_cast<float*>(smem + static_cast<size_t>(K) * 2);
+  for (int b = tid; b < K / 32; b += kR1Threads) {
+    const uint4* src = reinterpret_cast<const uint4*>(p.x) + 4 * b;
+    const int i = b >> 5, l = b & 31;
+    float sum = 0.f;
+#pragma unroll
+    for (int part = 0; part < 4; ++part) {
+      const uint4 v = __ldcg(src + part);
+      xs[(i * 4 + part) * 32 + l] = x_piece_to_frag<kFmtQ4>(v);
+      const uint32_t w4[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+      for (int e = 0; e < 4; ++e) sum += __uint_as_float(w4[e] << 16) + __uint_as_float(w4[e] & 0xFFFF0000u);
+    }
+    xsum[b] = sum;
+  }
+  __syncthreads();
+
+  constexpr int kLanesPerRow = 32 / RB;
+  for (; ra < r1; ra += 16 * RB) {
+    float acc[RB];
+#pragma unroll
+    for (int q = 0; q < RB; ++q) acc[q] = 0.f;
+#pragma unroll
+    for (int i = 0; i < KC; ++i) {
+      uint4 x[4];
+#pragma unroll
+      for (int part = 0; part < 4; ++part) x[part] = xs[(i * 4 + part) * 32 + lane];
+      const float xb = xsum[i * 32 + lane];
+#pragma unroll
+      for (int q = 0; q < RB; ++q)
+        acc[q] = fmaf(fmaf(-136.f, xb, q4_block_dot(wv[q][i], x)), bf16_bits_to_f32(sv[q][i]), acc[q]);
+    }
+    if (ra + 16 * RB < r1) load_rows(ra + 16 * RB);  // the warp's next rows, while it reduces
+    const float v = warp_sum_t<RB>(acc);
+    const int q = lane / kLanesPerRow;
+    if (lane % kLanesPerRow == 0 && ra + 16 * q < r1) p.y[ra + 16 * q] = __float2bfloat16(v);
+  }
+}
+
+template <int KC>
+cudaError_t launch_q4_r1(const R1Params& p, int grid, const LaunchCfg& cfg) {
+  const size_t smem = static_cast<size_t>(p.K) * 2 + static_cast<size_t>(p.K / 32) * 4;
+  constexpr int RB = KC <= 3 ? 4 : 2;  // rows per warp batch: RB * KC <= 12 loads in registers
+  auto kern = gemv_q4_r1_kernel<KC, RB>;
+  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
+  if (e != cudaSuccess) return e;
+  return launch_kernel(kern, dim3(grid), dim3(kR1Threads), smem, cfg, p);
+}
+
 }  // namespace
 
 cudaError_t launch_gemv_r1(int fmt, const bf16* x, const uint8_t* w, const void* sc, const float* gscale, int64_t N,
                            int K, bf16* y, const LaunchCfg& cfg) {
-  if (fmt != kFmtFp4 || N < 1 || K < 1024 || K % 1024 || K / 1024 > kR1MaxChunks) return cudaErrorNotSupported;
-  if ((reinterpret_cast<uintptr_t>(w) & 15) || (reinterpret_cast<uintptr_t>(sc) & 15) ||
+  if ((fmt != kFmtFp4 && fmt != kFmtQ4) || N < 1 || K < 1024 || K % 1024 || K / 1024 > kR1MaxChunks)
+    return cudaErrorNotSupported;
+  if ((reinterpret_cast<uintptr_t>(w) & 15) || (reinterpret_cast<uintptr_t>(sc) & (fmt == kFmtQ4 ? 1 : 15)) ||
       (reinterpret_cast<uintptr_t>(x) & 15))
     return cudaErrorNotSupported;
   R1Params p{x, w, static_cast<const uint8_t*>(sc), gscale, y, N, K, cfg.early_weights ? 1 : 0};
   const int grid = static_cast<int>(std::min<int64_t>(cfg.sms, (N + 15) / 16));
+  if (fmt == kFmtQ4) {
+    switch (K / 1024) {
+      case 1: return launch_q4_r1<1>(p, grid, cfg);
+      case 2: return launch_q4_r1<2>(p, grid, cfg);
+      case 3: return launch_q4_r1<3>(p, grid, cfg);
+      case 4: return launch_q4_r1<4>(p, grid, cfg);
+      case 5: return launch_q4_r1<5>(p, grid, cfg);
+      case 6: return launch_q4_r1<6>(p, grid, cfg);
+      case 7: return launch_q4_r1<7>(p, grid, cfg);
+      default: return launch_q4_r1<8>(p, grid, cfg);
+    }
+  }
   switch (K / 1024) {
     case 1: return launch_r1<1>(p, grid, cfg);
     case 2: return launch_r1<2>(p, grid, cfg);
