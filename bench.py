@@ -449,8 +449,8 @@ def sharded_measure(world, rank, device, op="MoeVerify", iq2=0, E=304, I=2304, R
     scratch = (torch.empty(P, I, dtype=torch.bfloat16, device=device),
                torch.empty(P, 1024, dtype=torch.float32, device=device),
                torch.empty(1 + P + 8 * P, dtype=torch.int32, device=device))
-    # the fused peer-memory reduction runs where its test runs: MoeVerify at 2 GPUs
-    reducer = PeerReducer(max_rows=R, device=device) if (verify and world == 2) else None
+    # the fused peer-memory reduction (MoeVerify; its parity is checked below on these ranks)
+    reducer = PeerReducer(max_rows=R, device=device) if verify else None
 
     def run(wts, mode):
         if mode == "peer":

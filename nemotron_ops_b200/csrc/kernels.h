@@ -67,9 +67,9 @@ cudaError_t launch_dequant(int fmt, int exact, const uint8_t* w, const void* sc,
 cudaError_t launch_relu2(const bf16* x, bf16* y, int64_t n, const LaunchCfg& cfg);
 
 // ---- NVLink peer reduction of the expert-sharded MoE --------------------------------------
-// bufs: device array of every rank's peer-visible buffer: 2 * stride fp32 partials, then
-// kPeerReduceCtas * world uint32 flag words (zero at start); epoch: this rank's
-// kPeerReduceCtas uint32 call counters (zero at start).
+// bufs: device array of every rank's peer-visible buffer: two halves of `world` slots of `stride`
+// fp32 partials (slot q holds rank q's partial), then kPeerReduceCtas * world uint32 flag words
+// (zero at start); epoch: this rank's kPeerReduceCtas uint32 call counters (zero at start).
 constexpr int kPeerReduceCtas = 16;
 struct PeerReduce {
   float* const* bufs;

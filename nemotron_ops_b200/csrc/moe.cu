@@ -557,13 +557,15 @@ __global__ void __launch_bounds__(256) moe_finalize_kernel(float* __restrict__ p
 }
 
 // Expert-sharded finalize fused with the all-reduce over NVLink peer memory (no NCCL): CTA c owns
-// a slice of the R x Nout outputs on every rank.  It writes this rank's partials of its slice into
-// this rank's peer-visible buffer (half e & 1 of it, e = the CTA's call count), publishes e to its
-// flag word on every peer (system-scope release), waits for every peer's e (acquire; bounded,
-// status bit on timeout), then sums the slice of all ranks' partials in rank order -- the same
-// order on every rank, so all ranks get identical bits -- and writes bf16.  A peer reads a buffer
-// half at call e only after both ranks finished call e - 1, so alternating halves keeps the next
-// call's writes off data still being read.  The call counters advance in device memory, so a
+// a slice of the R x Nout outputs on every rank.  It computes this rank's partials of its slice and
+// pushes them into slot `rank` of every rank's peer-visible buffer (half e & 1 of it, e = the CTA's
+// call count; posted stores, no remote loads), publishes e to its flag word on every peer
+// (system-scope release after a system fence), waits for every peer's e in its own flag words
+// (acquire; bounded, status bit on timeout), then sums the slice of all slots in rank order -- the
+// same order on every rank, so all ranks get identical bits -- from local memory and writes bf16.
+// A rank writes half h at call e only after every rank's flags for call e - 1 arrived, and a rank
+// sums half h of call e - 2 before it raises its flags for call e - 1, so alternating halves keeps
+// every write off data still being read.  The call counters advance in device memory, so a
 // replayed CUDA graph stays in step.
 __device__ __forceinline__ void st_release_sys(uint32_t* p, uint32_t v) {
   asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
@@ -573,9 +575,9 @@ __device__ __forceinline__ uint32_t ld_acquire_sys(const uint32_t* p) {
   asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
   return v;
 }
-// rank q's flag words: after its two halves of partials
+// rank q's flag words: after its two halves of world slots of partials
 __device__ __forceinline__ uint32_t* peer_flags(const PeerReduce& pr, int q) {
-  return reinterpret_cast<uint32_t*>(pr.bufs[q] + 2 * pr.stride);
+  return reinterpret_cast<uint32_t*>(pr.bufs[q] + 2 * pr.world * pr.stride);
 }
 
 __global__ void __launch_bounds__(256) moe_finalize_allreduce_kernel(float* __restrict__ part, int round_part,
@@ -596,15 +598,16 @@ __global__ void __launch_bounds__(256) moe_finalize_allreduce_kernel(float* __re
   }
   __syncthreads();
   const uint32_t e = s_e;
-  const int64_t half = static_cast<int64_t>(e & 1u) * pr.stride;
-  float* mine = pr.bufs[pr.rank] + half;
+  const int64_t half = static_cast<int64_t>(e & 1u) * pr.world * pr.stride;
+  const int64_t slot = half + static_cast<int64_t>(pr.rank) * pr.stride;
   for (int64_t i = i0 + tid; i < i1; i += blockDim.x) {
     const int t = static_cast<int>(i / Nout), col = static_cast<int>(i % Nout);
-    mine[i] = local_partial(part, round_part, w, idx, t, col, topk, Nout, e_begin, e_end);
+    const float v = local_partial(part, round_part, w, idx, t, col, topk, Nout, e_begin, e_end);
+    for (int q = 0; q < pr.world; ++q) pr.bufs[q][slot + i] = v;  // this rank's slot on every rank
   }
   __syncthreads();
   if (tid == 0) {
-    __threadfence_system();  // this CTA's partials are visible to the peers before its flag
+    __threadfence_system();  // the CTA's pushed partials are visible to the peers before its flags
     for (int q = 0; q < pr.world; ++q)
       if (q != pr.rank) st_release_sys(peer_flags(pr, q) + c * pr.world + pr.rank, e);
     const unsigned long long t0 = globaltimer();
@@ -623,9 +626,10 @@ __global__ void __launch_bounds__(256) moe_finalize_allreduce_kernel(float* __re
   }
   __syncthreads();
   if (!s_ok) return;
+  const float* mine = pr.bufs[pr.rank] + half;
   for (int64_t i = i0 + tid; i < i1; i += blockDim.x) {
     float s = 0.f;
-    for (int q = 0; q < pr.world; ++q) s += q == pr.rank ? mine[i] : __ldcg(pr.bufs[q] + half + i);
+    for (int q = 0; q < pr.world; ++q) s += __ldcg(mine + static_cast<int64_t>(q) * pr.stride + i);
     out[i] = __float2bfloat16(s);
   }
 }

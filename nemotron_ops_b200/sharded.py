@@ -33,8 +33,8 @@ def expert_range(num_experts: int, rank: int, world: int):
 class PeerReducer:
     """Peer-visible buffers of ``bolt_moe_verify_shard_allreduce`` for the ranks of ``group``
     (CUDA, one process per GPU): torch symmetric memory maps every rank's buffer -- two halves of
-    ``max_rows * 1024`` fp32 partials, then the flag words, zeroed here -- into every peer; the
-    call counters are this rank's.  Only plain peer loads and stores touch it, so torch's NVLink
+    ``world`` slots of ``max_rows * 1024`` fp32 partials (slot q receives rank q's partial), then the
+    flag words, zeroed here -- into every peer; the call counters are this rank's.  Only plain peer loads and stores touch it, so torch's NVLink
     multicast binding is switched off (unless the caller set TORCH_SYMM_MEM_DISABLE_MULTICAST).
     Create it on every rank (a collective) before stream capture, and make the same sequence of
     calls on every rank."""
@@ -48,7 +48,7 @@ class PeerReducer:
         group = group if group is not None else dist.group.WORLD
         world = dist.get_world_size(group)
         self.half = int(max_rows) * 1024
-        self.buf = symm_mem.empty(2 * self.half + self.CTAS * world, dtype=torch.float32, device=device)
+        self.buf = symm_mem.empty(2 * world * self.half + self.CTAS * world, dtype=torch.float32, device=device)
         self.buf.zero_()
         torch.cuda.synchronize(device)
         self.handle = symm_mem.rendezvous(self.buf, group)
