@@ -23,7 +23,8 @@ namespace {
 // all issued before the first use, so one pass of the whole grid puts the full 2.5 MB gate of
 // E = 304, K = 4096 in flight at once.  The pass's activation rows (at most 8 x 4096 bf16 = 64 KB)
 // are staged in shared memory once per CTA instead of being re-read from L2 by every warp.  The
-// row's four warp sums are added in warp order, so results do not depend on scheduling.
+// row's four warp sums are added in warp order, so results do not depend on scheduling.  Before its
+// dependency wait a CTA only pulls its gate rows into L2 (coherent with an upstream writer).
 constexpr int kRouteExperts = 2;                            // gate rows per CTA
 constexpr int kRouteRowLanes = 128;                         // lanes per gate row
 constexpr int kRouteVec = 4;                                // 16-byte gate vectors per lane and pass
@@ -52,6 +53,10 @@ __global__ void __launch_bounds__(kRouteThreads, 2)
   const int V = K >> 3;  // 16-byte vectors per row (K % 256 == 0)
   const uint4* wr = reinterpret_cast<const uint4*>(gw) + static_cast<int64_t>(e < E ? e : E - 1) * V;
   const uint4* xv = reinterpret_cast<const uint4*>(x);
+  if (!early && threadIdx.x == 0) {  // pull the CTA's gate rows into L2 while the previous kernel runs
+    const int e0 = blockIdx.x * kRouteExperts, ne = min(kRouteExperts, E - e0);
+    if (ne > 0) prefetch_span_l2(gw + static_cast<int64_t>(e0) * K, static_cast<uint64_t>(ne) * K * 2);
+  }
   bool waited = false;
   for (int r0 = 0; r0 < R; r0 += RB) {
     const int rows = min(RB, R - r0);
