@@ -132,10 +132,10 @@ cudaError_t launch_moe_finalize(float* part, int round_part, const float* w, con
 cudaError_t launch_moe_finalize_allreduce(float* part, int round_part, const float* w, const int* idx, int R,
                                           int topk, int e_begin, int e_end, const PeerReduce& pr, bf16* out,
                                           const LaunchCfg& cfg);
-// MoeVerify with int4 experts on the register-streaming tensor-core kernels (moe_vstream.cu; R <= 8,
-// R * topk <= 128, I % 128 == 0, 16-byte aligned z, weights and h): cudaErrorNotSupported, with
-// nothing launched, for shapes they do not take.
-cudaError_t launch_moe_verify_stream(const bf16* z, const int* idx, const float* w, const uint8_t* fc1_w,
+// MoeVerify (fmt kFmtQ4, kFmtIq2Lut or kFmtIq2N) on the register-streaming tensor-core kernels
+// (moe_vstream.cu; R <= 8, R * topk <= 128, I % 256 == 0, 16-byte aligned z, weights and h):
+// cudaErrorNotSupported, with nothing launched, for shapes they do not take.
+cudaError_t launch_moe_verify_stream(int fmt, const bf16* z, const int* idx, const float* w, const uint8_t* fc1_w,
                                      const bf16* fc1_s, const uint8_t* fc2_w, const bf16* fc2_s, int R, int E, int I,
                                      int topk, int e_begin, int e_end, bf16* out, bf16* h, float* part, int* meta,
                                      float* out_partial, const LaunchCfg& cfg, const PeerReduce* pr);

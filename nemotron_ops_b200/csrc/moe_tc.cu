@@ -736,8 +736,8 @@ cudaError_t launch_moe_verify(int fmt, const bf16* z, const int* idx, const floa
                               int topk, int e_begin, int e_end, bf16* out, bf16* h, float* part, int* meta,
                               float* out_partial, const LaunchCfg& cfg, const PeerReduce* pr) {
   const int P = R * topk;
-  if (fmt == kFmtQ4) {  // register-streaming tensor-core kernels (moe_vstream.cu) where they take the shape
-    const cudaError_t e = launch_moe_verify_stream(z, idx, w, fc1_w, fc1_s, fc2_w, fc2_s, R, E, I, topk, e_begin,
+  {  // register-streaming tensor-core kernels (moe_vstream.cu) where they take the shape
+    const cudaError_t e = launch_moe_verify_stream(fmt, z, idx, w, fc1_w, fc1_s, fc2_w, fc2_s, R, E, I, topk, e_begin,
                                                    e_end, out, h, part, meta, out_partial, cfg, pr);
     if (e != cudaErrorNotSupported) return e;
   }

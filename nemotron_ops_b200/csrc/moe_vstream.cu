@@ -1,4 +1,4 @@
-// MoeVerify with int4 experts on register-streaming tensor-core kernels (the reference op is
+// MoeVerify (int4 and both iq2 formats) on register-streaming tensor-core kernels (the reference op is
 // MoeVerify's ComputeV2, src/bolt_ops.cu:1178-1257, with MoeGroupKernel :1083-1112 and the grouped
 // expert GEMMs).  Weight contract of the tensor-core path: W = bf16((q - 8) * bf16(s)), bf16
 // activations, fp32 sums,
@@ -34,6 +34,7 @@ __device__ __forceinline__ int bx_index(int j, int h, int q, int c) { return ((j
 
 // one 32-k block (four 16-byte pieces of 8 k, row-major bf16) -> the B fragments of its two
 // 16-k halves for lane c = blk & 3 of chunk j = blk >> 2
+template <int FMT>
 __device__ __forceinline__ void stage_block(uint4* row, int blk, const uint4 (&v)[4]) {
   const int j = blk >> 2, c = blk & 3;
 #pragma unroll
@@ -41,7 +42,7 @@ __device__ __forceinline__ void stage_block(uint4* row, int blk, const uint4 (&v
     const uint32_t x16[8] = {v[2 * h].x, v[2 * h].y, v[2 * h].z, v[2 * h].w,
                              v[2 * h + 1].x, v[2 * h + 1].y, v[2 * h + 1].z, v[2 * h + 1].w};
     uint32_t b[8];
-    make_b_frags<kFmtQ4>(x16, b);
+    make_b_frags<FMT>(x16, b);
     row[bx_index(j, h, 0, c)] = make_uint4(b[0], b[1], b[2], b[3]);
     row[bx_index(j, h, 1, c)] = make_uint4(b[4], b[5], b[6], b[7]);
   }
@@ -61,8 +62,18 @@ __device__ __forceinline__ void decode_q4_mma(uint32_t wx, uint32_t wy, __nv_bfl
   }
 }
 
-template <int FC>
+__device__ __forceinline__ uint2 ld_stream8(const void* p) {
+  uint2 v;
+  asm volatile("ld.global.nc.L1::no_allocate.v2.u32 {%0, %1}, [%2];" : "=r"(v.x), "=r"(v.y) : "l"(p));
+  return v;
+}
+
+// FMT: kFmtQ4 (int4), kFmtIq2Lut (iq2 = 1: 4-bit LUT codes, bf16 block-32 scales) or kFmtIq2N
+// (iq2 = 2: 8-byte IQ2_XXS records per 32 k, an fp16 scale per 256 k)
+template <int FC, int FMT>
 __global__ void __launch_bounds__(kMsThreads, 1) moe_vstream_kernel(const MsParams p) {
+  constexpr bool kIq2n = FMT == kFmtIq2N;
+  __shared__ __align__(16) uint32_t grid_s[kIq2n ? 1024 : 4];  // IQ2_XXS codebook (bf16 pairs)
   extern __shared__ __align__(16) uint8_t dsm[];
   __shared__ Groups g;
   __shared__ int tok_pair[kVsMaxSpan][kVsTok];  // fc2: pair of (group slot, token), -1: none
@@ -72,11 +83,13 @@ __global__ void __launch_bounds__(kMsThreads, 1) moe_vstream_kernel(const MsPara
   const int I = p.I;
   const int K = FC == 1 ? 1024 : I, NR = FC == 1 ? I : 1024, nch = K / 128;
   const int spt = (nch + kVsKG - 1) / kVsKG, TE = NR / 16;
-  const int64_t wrow = K / 2, srow = K / 32;
+  const int64_t wrow = kIq2n ? K / 4 : K / 2, srow = kIq2n ? K / 256 : K / 32;
   const uint8_t* W = FC == 1 ? p.w1 : p.w2;
   const uint16_t* S = reinterpret_cast<const uint16_t*>(FC == 1 ? p.s1 : p.s2);
   const int rstride = nch * 16 + 4;  // uint4 per staged source row
 
+  if constexpr (kIq2n)
+    for (int i = tid; i < 1024; i += kMsThreads) grid_s[i] = kIq2xxsGridBf16x2[i];
   uint4 zv[4];
   const bool zjob = FC == 1 && tid < p.R * 32;
   if constexpr (FC == 1) {
@@ -128,17 +141,26 @@ __global__ void __launch_bounds__(kMsThreads, 1) moe_vstream_kernel(const MsPara
     const int nj = min(kVsKG, nch - u.kg * kVsKG);
     const int64_t row = static_cast<int64_t>(g.gexp[u.gi]) * NR + u.rt * 16 + gq;
     const int blk0 = 4 * kVsKG * u.kg + c;
-    const uint8_t* w0 = W + row * wrow + 16 * blk0;
+    const uint8_t* w0 = W + row * wrow + (kIq2n ? 8 : 16) * blk0;
     const uint8_t* w1 = w0 + 8 * wrow;
-    const uint16_t* s0 = S + row * srow + blk0;
+    const uint16_t* s0 = S + row * srow + (kIq2n ? 0 : blk0);
     const uint16_t* s1 = s0 + 8 * srow;
 #pragma unroll
     for (int jj = 0; jj < kVsKG; ++jj)
       if (jj < nj) {
-        w[jj][0] = ld_stream(w0 + 64 * jj);
-        w[jj][1] = ld_stream(w1 + 64 * jj);
-        s[jj][0] = ld_u16(s0 + 4 * jj);
-        s[jj][1] = ld_u16(s1 + 4 * jj);
+        if constexpr (kIq2n) {  // one 8-byte record per row; the scale of its 256-k superblock
+          const uint2 a = ld_stream8(w0 + 32 * jj), b = ld_stream8(w1 + 32 * jj);
+          w[jj][0] = make_uint4(a.x, a.y, 0u, 0u);
+          w[jj][1] = make_uint4(b.x, b.y, 0u, 0u);
+          const int sb = (kVsKG * u.kg + jj) >> 1;
+          s[jj][0] = ld_u16(s0 + sb);
+          s[jj][1] = ld_u16(s1 + sb);
+        } else {
+          w[jj][0] = ld_stream(w0 + 64 * jj);
+          w[jj][1] = ld_stream(w1 + 64 * jj);
+          s[jj][0] = ld_u16(s0 + 4 * jj);
+          s[jj][1] = ld_u16(s1 + 4 * jj);
+        }
       }
   };
   if (warp < nsu) issue(ua, wq[0], sq[0]);
@@ -173,7 +195,7 @@ __global__ void __launch_bounds__(kMsThreads, 1) moe_vstream_kernel(const MsPara
   uint4* bx = reinterpret_cast<uint4*>(dsm);
   int span = 0;
   if constexpr (FC == 1) {
-    if (zjob) stage_block(bx + (tid >> 5) * rstride, tid & 31, zv);
+    if (zjob) stage_block<FMT>(bx + (tid >> 5) * rstride, tid & 31, zv);
   } else {
     span = nsu > 0 ? (t1 - 1) / TE - gA + 1 : 0;
     if (tid < kVsMaxSpan * kVsTok) tok_pair[tid / kVsTok][tid % kVsTok] = -1;
@@ -198,7 +220,7 @@ __global__ void __launch_bounds__(kMsThreads, 1) moe_vstream_kernel(const MsPara
 #pragma unroll
         for (int i = 0; i < 4; ++i) v[i] = make_uint4(0u, 0u, 0u, 0u);
       }
-      stage_block(bx + (sl * kVsTok + t) * rstride, blk, v);
+      stage_block<FMT>(bx + (sl * kVsTok + t) * rstride, blk, v);
     }
   }
   // a zero row after the staged rows (B of tokens without a pair of the expert), then the sums
@@ -237,8 +259,18 @@ __global__ void __launch_bounds__(kMsThreads, 1) moe_vstream_kernel(const MsPara
 #pragma unroll
         for (int h = 0; h < 2; ++h) {
           uint32_t a0[8], a1[8];
-          decode_q4_mma(h ? w[jj][0].z : w[jj][0].x, h ? w[jj][0].w : w[jj][0].y, s0, a0);
-          decode_q4_mma(h ? w[jj][1].z : w[jj][1].x, h ? w[jj][1].w : w[jj][1].y, s1, a1);
+          if constexpr (FMT == kFmtQ4) {
+            decode_q4_mma(h ? w[jj][0].z : w[jj][0].x, h ? w[jj][0].w : w[jj][0].y, s0, a0);
+            decode_q4_mma(h ? w[jj][1].z : w[jj][1].x, h ? w[jj][1].w : w[jj][1].y, s1, a1);
+          } else if constexpr (kIq2n) {  // half h of the record: its groups 2 h and 2 h + 1
+            decode_row<kFmtIq2N>(RawRow{w[jj][0], s[jj][0]}, h, grid_s, a0);
+            decode_row<kFmtIq2N>(RawRow{w[jj][1], s[jj][1]}, h, grid_s, a1);
+          } else {
+            decode_row<FMT>(RawRow{make_uint4(h ? w[jj][0].z : w[jj][0].x, h ? w[jj][0].w : w[jj][0].y, 0u, 0u),
+                                   s[jj][0]}, 0, nullptr, a0);
+            decode_row<FMT>(RawRow{make_uint4(h ? w[jj][1].z : w[jj][1].x, h ? w[jj][1].w : w[jj][1].y, 0u, 0u),
+                                   s[jj][1]}, 0, nullptr, a1);
+          }
           const uint4 lo = brow[bx_index(jj, h, 0, 0)], hi = brow[bx_index(jj, h, 1, 0)];
           const uint32_t b[8] = {lo.x, lo.y, lo.z, lo.w, hi.x, hi.y, hi.z, hi.w};
 #pragma unroll
@@ -300,17 +332,30 @@ __global__ void __launch_bounds__(kMsThreads, 1) moe_vstream_kernel(const MsPara
   }
 }
 
-std::atomic<size_t> g_vs_smem[2] = {{48 * 1024}, {48 * 1024}};
+std::atomic<size_t> g_vs_smem[3][2] = {{{48 * 1024}, {48 * 1024}}, {{48 * 1024}, {48 * 1024}}, {{48 * 1024}, {48 * 1024}}};
+
+template <int FMT>
+cudaError_t launch_layers(const MsParams& p, size_t smem1, size_t smem2, const LaunchCfg& c1, const LaunchCfg& c2) {
+  std::atomic<size_t>* cur = g_vs_smem[FMT == kFmtQ4 ? 0 : FMT == kFmtIq2N ? 1 : 2];
+  cudaError_t e = allow_smem(moe_vstream_kernel<1, FMT>, smem1, cur[0]);
+  if (e != cudaSuccess) return e;
+  e = allow_smem(moe_vstream_kernel<2, FMT>, smem2, cur[1]);
+  if (e != cudaSuccess) return e;
+  e = launch_kernel(moe_vstream_kernel<1, FMT>, dim3(c1.sms), dim3(kMsThreads), smem1, c1, p);
+  if (e != cudaSuccess) return e;
+  return launch_kernel(moe_vstream_kernel<2, FMT>, dim3(c1.sms), dim3(kMsThreads), smem2, c2, p);
+}
 constexpr size_t kVsSmemCap = 200 * 1024;
 
 }  // namespace
 
-cudaError_t launch_moe_verify_stream(const bf16* z, const int* idx, const float* w, const uint8_t* fc1_w,
+cudaError_t launch_moe_verify_stream(int fmt, const bf16* z, const int* idx, const float* w, const uint8_t* fc1_w,
                                      const bf16* fc1_s, const uint8_t* fc2_w, const bf16* fc2_s, int R, int E, int I,
                                      int topk, int e_begin, int e_end, bf16* out, bf16* h, float* part, int* meta,
                                      float* out_partial, const LaunchCfg& cfg, const PeerReduce* pr) {
   const int P = R * topk;
-  if (R < 1 || R > kVsTok || P > kMsMaxP || I < 128 || I % 128) return cudaErrorNotSupported;
+  if (fmt != kFmtQ4 && fmt != kFmtIq2Lut && fmt != kFmtIq2N) return cudaErrorNotSupported;
+  if (R < 1 || R > kVsTok || P > kMsMaxP || I < 256 || I % 256) return cudaErrorNotSupported;
   const auto al = [](const void* q) { return (reinterpret_cast<uintptr_t>(q) & 15) == 0; };
   if (!al(z) || !al(fc1_w) || !al(fc2_w) || !al(h) || (reinterpret_cast<uintptr_t>(fc1_s) & 1) ||
       (reinterpret_cast<uintptr_t>(fc2_s) & 1))
@@ -332,17 +377,11 @@ cudaError_t launch_moe_verify_stream(const bf16* z, const int* idx, const float*
   if (smem1 > kVsSmemCap || smem2 > kVsSmemCap || span2 > kVsMaxSpan) return cudaErrorNotSupported;
   MsParams p{z, idx, w, fc1_w, fc1_s, fc2_w, fc2_s, h, part, out, out_partial, meta, R, P, topk, E, I, e_begin, e_end,
              0};
-  static std::atomic<size_t>* cur = g_vs_smem;
-  auto set_smem = [&](auto kern, size_t bytes, std::atomic<size_t>& c) { return allow_smem(kern, bytes, c); };
-  cudaError_t e = set_smem(moe_vstream_kernel<1>, smem1, cur[0]);
-  if (e != cudaSuccess) return e;
-  e = set_smem(moe_vstream_kernel<2>, smem2, cur[1]);
-  if (e != cudaSuccess) return e;
-  e = launch_kernel(moe_vstream_kernel<1>, dim3(G), dim3(kMsThreads), smem1, cfg, p);
-  if (e != cudaSuccess) return e;
   LaunchCfg c2 = cfg;
   c2.pdl = true;  // same op: each kernel waits for its predecessor with griddepcontrol.wait
-  e = launch_kernel(moe_vstream_kernel<2>, dim3(G), dim3(kMsThreads), smem2, c2, p);
+  cudaError_t e = fmt == kFmtQ4      ? launch_layers<kFmtQ4>(p, smem1, smem2, cfg, c2)
+                  : fmt == kFmtIq2N  ? launch_layers<kFmtIq2N>(p, smem1, smem2, cfg, c2)
+                                     : launch_layers<kFmtIq2Lut>(p, smem1, smem2, cfg, c2);
   if (e != cudaSuccess) return e;
   if (pr != nullptr) return launch_moe_finalize_allreduce(part, 0, w, idx, R, topk, e_begin, e_end, *pr, out, c2);
   return launch_moe_finalize(part, 0, w, idx, R, topk, e_begin, e_end, out, out_partial, c2);
