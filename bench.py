@@ -176,7 +176,7 @@ def _moe_workload(op_name, R, iq2=0, E=304, I=2304, topk=8, route=False):
         # (+ router logits, selection)
         kern = (2 if op_name == "MoeDecode" else 3) + (2 if route else 0)
         main_kernel = ("moe_stream_fc1_kernel + moe_stream_fc2_kernel" if op_name == "MoeDecode" else
-                       "moe_vstream_kernel" if iq2 == 0 else "moe_umma_kernel")
+                       "moe_vstream_kernel")
         return dict(calls=calls, bytes=nbytes, kernels=kern, h2d=R * 1024 * 2,
                     d2h=R * 1024 * 2, e2e=e2e, cpu=cpu, cpu_sample=R * topk, dtype="f32" if op_name == "MoeDecode"
                     else "bf16", unique_experts=uniq, kernel=main_kernel)
