@@ -581,6 +581,10 @@ cudaError_t launch_gemv_mma(int fmt, const bf16* x, int R, const uint8_t* w, con
                             int64_t N, int K, bf16* y, const LaunchCfg& cfg) {
   const bool bc = R == 1 && (fmt == kFmtQ4 || fmt == kFmtFp4);
   if (bc && fmt == kFmtQ4 && K % 256) return cudaErrorInvalidValue;
+  if (R == 1 && fmt == kFmtIq2N) {  // the register-streaming IQ2_XXS kernel (gemv_r1.cu)
+    const cudaError_t e = launch_gemv_r1(fmt, x, w, sc, gscale, N, K, y, cfg);
+    if (e != cudaErrorNotSupported) return e;
+  }
   if (bc) {  // the register-streaming block-column kernel when it takes the shape (gemv_r1.cu)
     const cudaError_t e = launch_gemv_r1(fmt, x, w, sc, gscale, N, K, y, cfg);
     if (e != cudaErrorNotSupported) return e;

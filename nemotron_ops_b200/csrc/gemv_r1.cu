@@ -18,7 +18,7 @@
 //  * programmatic dependent launch: weights and scales are read after griddepcontrol.wait (an
 //    earlier kernel may write them); before it the CTA only pulls its rows into L2, which stays
 //    coherent with such writes.  With early weights the loads themselves go before the wait.
-// The file also holds the Q4Gemv (int4) R = 1 kernel on the same streaming layout (below).
+// The file also holds the Q4Gemv int4 and IQ2_XXS R = 1 kernels on the same streaming layout (below).
 #include "mma_decode.cuh"
 
 namespace bolt {
@@ -319,10 +319,143 @@ cudaError_t launch_q4_r1(const R1Params& p, int grid, const LaunchCfg& cfg) {
   return launch_kernel(kern, dim3(grid), dim3(kR1Threads), smem, cfg, p);
 }
 
+// ------------------------------------------------------------------------------------------
+// Q4Gemv iq2 = 2 (native IQ2_XXS records) at R = 1.  Weight contract of the reference's iq2 path:
+// w = +-bf16(mag * bf16(d * (0.5 + s4) * 0.25)) (the decode of mma_decode.cuh), products with x
+// exact and summed in fp32.  A row is K / 4 bytes (an 8-byte record per 32 k); lane l reads 16
+// bytes (two records, 64 k) per 2048-k chunk and the fp16 scale of their 256-k superblock; a warp
+// takes RB rows at a time and shares each activation chunk among them (x in shared memory as
+// [chunk][8-k piece][lane], so a warp's 16-byte reads are contiguous); the codebook sits in shared
+// memory; the RB row sums meet in one butterfly reduction.
+// ------------------------------------------------------------------------------------------
+// One IQ2_XXS record (32 k: four grid indices in idx4; four 7-bit sign patterns and the 4-bit
+// sub-scale in sg) -> 16 bf16 pairs in k order, each +-bf16(mag * bf16(d * (0.5 + s4) * 0.25)):
+// the arithmetic of decode_row<kFmtIq2N>, with the block scale formed once per record.
+__device__ __forceinline__ void iq2n_record(uint32_t idx4, uint32_t sg, uint32_t dbits, const uint32_t* grid,
+                                            uint32_t (&out)[16]) {
+  const float d = __half2float(__ushort_as_half(static_cast<unsigned short>(dbits)));
+  const float db = d * (0.5f + static_cast<float>(sg >> 28)) * 0.25f;
+  const __nv_bfloat162 s2 = __bfloat162bfloat162(__float2bfloat16_rn(db));
+#pragma unroll
+  for (int gi = 0; gi < 4; ++gi) {
+    const uint4 gv = *reinterpret_cast<const uint4*>(grid + 4 * ((idx4 >> (8 * gi)) & 0xFFu));
+    uint32_t pat = (sg >> (7 * gi)) & 127u;
+    pat |= (__popc(pat) & 1u) << 7;
+    const uint32_t gw[4] = {gv.x, gv.y, gv.z, gv.w};
+#pragma unroll
+    for (int j = 0; j < 4; ++j) out[4 * gi + j] = bf2_bits(__hmul2(bits_bf2(gw[j] ^ iq2_sign_mask(pat, j)), s2));
+  }
+}
+
+template <int KC, int RB>
+__global__ void __launch_bounds__(kR1Threads, 1) gemv_iq2n_r1_kernel(const R1Params p) {
+  extern __shared__ __align__(16) uint8_t smem[];  // x: [chunk][piece 0..7][lane] 16-byte pieces
+  __shared__ __align__(16) uint32_t grid_s[1024];
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int K = p.K;
+  const int64_t rb = K / 4, srb = K / 256;  // bytes per weight row, scales per row
+  const int64_t r0 = static_cast<int64_t>(blockIdx.x) * p.N / gridDim.x;
+  const int64_t r1 = static_cast<int64_t>(blockIdx.x + 1) * p.N / gridDim.x;
+  const uint16_t* sc = reinterpret_cast<const uint16_t*>(p.sc);
+  pdl_trigger();
+  for (int i = tid; i < 1024; i += kR1Threads) grid_s[i] = kIq2xxsGridBf16x2[i];
+
+  uint4 wv[RB][KC];
+  uint32_t sv[RB][KC];
+  auto load_rows = [&](int64_t ra) {
+#pragma unroll
+    for (int q = 0; q < RB; ++q) {
+      const int64_t r = ra + 16 * q;
+      if (r < r1) {
+        const uint8_t* wr = p.w + r * rb + 16 * lane;
+        const uint16_t* sr = sc + r * srb + (lane >> 2);
+#pragma unroll
+        for (int i = 0; i < KC; ++i) {
+          wv[q][i] = ldg_stream(wr + 512 * i);
+          sv[q][i] = ldg_u16(sr + 8 * i);
+        }
+      }
+    }
+  };
+  int64_t ra = r0 + warp;
+  if (p.early_weights) {
+    load_rows(ra);
+  } else if (tid == 0) {  // the CTA's rows are contiguous: pull them into L2 during the previous kernel
+    prefetch_span_l2(p.w + r0 * rb, static_cast<uint64_t>(r1 - r0) * rb);
+  }
+  pdl_wait();
+  if (!p.early_weights) load_rows(ra);
+
+  uint4* xs = reinterpret_cast<uint4*>(smem);
+  for (int q = tid; q < K / 8; q += kR1Threads) {  // 8-k piece q -> chunk q / 256, lane (q / 8) % 32, piece q % 8
+    const int i = q >> 8, l = (q >> 3) & 31, piece = q & 7;
+    xs[(i * 8 + piece) * 32 + l] = __ldcg(reinterpret_cast<const uint4*>(p.x) + q);
+  }
+  __syncthreads();
+
+  constexpr int kLanesPerRow = 32 / RB;
+  for (; ra < r1; ra += 16 * RB) {
+    float acc[RB];
+#pragma unroll
+    for (int q = 0; q < RB; ++q) acc[q] = 0.f;
+#pragma unroll
+    for (int i = 0; i < KC; ++i) {
+      uint32_t x[32];  // the lane's 64 k as bf16 pairs
+#pragma unroll
+      for (int piece = 0; piece < 8; ++piece) {
+        const uint4 v = xs[(i * 8 + piece) * 32 + lane];
+        x[4 * piece] = v.x;
+        x[4 * piece + 1] = v.y;
+        x[4 * piece + 2] = v.z;
+        x[4 * piece + 3] = v.w;
+      }
+#pragma unroll
+      for (int q = 0; q < RB; ++q) {
+        float a = 0.f, b = 0.f;
+#pragma unroll
+        for (int rec = 0; rec < 2; ++rec) {
+          uint32_t d[16];
+          iq2n_record(rec ? wv[q][i].z : wv[q][i].x, rec ? wv[q][i].w : wv[q][i].y, sv[q][i], grid_s, d);
+#pragma unroll
+          for (int j = 0; j < 16; ++j) fma2_bf16_f32r(d[j], x[16 * rec + j], a, b);
+        }
+        acc[q] += a + b;
+      }
+    }
+    if (ra + 16 * RB < r1) load_rows(ra + 16 * RB);  // the warp's next rows, while it reduces
+    const float v = warp_sum_t<RB>(acc);
+    const int q = lane / kLanesPerRow;
+    if (lane % kLanesPerRow == 0 && ra + 16 * q < r1) p.y[ra + 16 * q] = __float2bfloat16(v);
+  }
+}
+
+template <int KC>
+cudaError_t launch_iq2n_r1(const R1Params& p, int grid, const LaunchCfg& cfg) {
+  const size_t smem = static_cast<size_t>(p.K) * 2;
+  constexpr int RB = KC <= 1 ? 4 : 2;  // rows per warp batch without spilling
+  auto kern = gemv_iq2n_r1_kernel<KC, RB>;
+  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
+  if (e != cudaSuccess) return e;
+  return launch_kernel(kern, dim3(grid), dim3(kR1Threads), smem, cfg, p);
+}
+
 }  // namespace
 
 cudaError_t launch_gemv_r1(int fmt, const bf16* x, const uint8_t* w, const void* sc, const float* gscale, int64_t N,
                            int K, bf16* y, const LaunchCfg& cfg) {
+  if (fmt == kFmtIq2N) {
+    if (N < 1 || K < 2048 || K % 2048 || K / 2048 > 4 || (reinterpret_cast<uintptr_t>(w) & 15) ||
+        (reinterpret_cast<uintptr_t>(sc) & 1) || (reinterpret_cast<uintptr_t>(x) & 15))
+      return cudaErrorNotSupported;
+    const R1Params q{x, w, static_cast<const uint8_t*>(sc), gscale, y, N, K, cfg.early_weights ? 1 : 0};
+    const int grid = static_cast<int>(std::min<int64_t>(cfg.sms, (N + 15) / 16));
+    switch (K / 2048) {
+      case 1: return launch_iq2n_r1<1>(q, grid, cfg);
+      case 2: return launch_iq2n_r1<2>(q, grid, cfg);
+      case 3: return launch_iq2n_r1<3>(q, grid, cfg);
+      default: return launch_iq2n_r1<4>(q, grid, cfg);
+    }
+  }
   if ((fmt != kFmtFp4 && fmt != kFmtQ4) || N < 1 || K < 1024 || K % 1024 || K / 1024 > kR1MaxChunks)
     return cudaErrorNotSupported;
   if ((reinterpret_cast<uintptr_t>(w) & 15) || (reinterpret_cast<uintptr_t>(sc) & (fmt == kFmtQ4 ? 1 : 15)) ||

@@ -52,7 +52,7 @@ enum WeightFmt : int { kFmtQ8 = 0, kFmtQ4 = 1, kFmtFp4 = 2, kFmtIq2Lut = 3, kFmt
 cudaError_t launch_gemv_mma(int fmt, const bf16* x, int R, const uint8_t* w, const void* sc, const float* gscale,
                             int64_t N, int K, bf16* y, const LaunchCfg& cfg);
 
-// R = 1 streaming GEMV (fmt kFmtFp4 or kFmtQ4, 16-byte aligned tensors): cudaErrorNotSupported,
+// R = 1 streaming GEMV (fmt kFmtFp4, kFmtQ4 or kFmtIq2N, 16-byte aligned tensors): cudaErrorNotSupported,
 // with nothing launched, for shapes it does not take (gemv_r1.cu).
 cudaError_t launch_gemv_r1(int fmt, const bf16* x, const uint8_t* w, const void* sc, const float* gscale, int64_t N,
                            int K, bf16* y, const LaunchCfg& cfg);
