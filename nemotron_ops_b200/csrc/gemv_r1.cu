@@ -326,19 +326,22 @@ cudaError_t launch_q4_r1(const R1Params& p, int grid, const LaunchCfg& cfg) {
 // bytes (two records, 64 k) per 2048-k chunk and the fp16 scale of their 256-k superblock; a warp
 // takes RB rows at a time and shares each activation chunk among them (x in shared memory as
 // [chunk][8-k piece][lane], so a warp's 16-byte reads are contiguous); the codebook sits in shared
-// memory; the RB row sums meet in one butterfly reduction.
+// memory in 8 bank-group copies (conflict-free lookups); the RB row sums meet in one butterfly reduction.
 // ------------------------------------------------------------------------------------------
 // One IQ2_XXS record (32 k: four grid indices in idx4; four 7-bit sign patterns and the 4-bit
 // sub-scale in sg) -> 16 bf16 pairs in k order, each +-bf16(mag * bf16(d * (0.5 + s4) * 0.25)):
 // the arithmetic of decode_row<kFmtIq2N>, with the block scale formed once per record.
-__device__ __forceinline__ void iq2n_record(uint32_t idx4, uint32_t sg, uint32_t dbits, const uint32_t* grid,
+// grid: the codebook in 8 bank-group copies, entry e of copy c at uint4 index 8 e + c; lane l reads
+// copy l % 8, so the 8 lanes of a shared-memory phase never share a bank group.
+__device__ __forceinline__ void iq2n_record(uint32_t idx4, uint32_t sg, uint32_t dbits, const uint4* grid,
                                             uint32_t (&out)[16]) {
+  const int copy = threadIdx.x & 7;
   const float d = __half2float(__ushort_as_half(static_cast<unsigned short>(dbits)));
   const float db = d * (0.5f + static_cast<float>(sg >> 28)) * 0.25f;
   const __nv_bfloat162 s2 = __bfloat162bfloat162(__float2bfloat16_rn(db));
 #pragma unroll
   for (int gi = 0; gi < 4; ++gi) {
-    const uint4 gv = *reinterpret_cast<const uint4*>(grid + 4 * ((idx4 >> (8 * gi)) & 0xFFu));
+    const uint4 gv = grid[8 * ((idx4 >> (8 * gi)) & 0xFFu) + copy];
     uint32_t pat = (sg >> (7 * gi)) & 127u;
     pat |= (__popc(pat) & 1u) << 7;
     const uint32_t gw[4] = {gv.x, gv.y, gv.z, gv.w};
@@ -350,7 +353,7 @@ __device__ __forceinline__ void iq2n_record(uint32_t idx4, uint32_t sg, uint32_t
 template <int KC, int RB>
 __global__ void __launch_bounds__(kR1Threads, 1) gemv_iq2n_r1_kernel(const R1Params p) {
   extern __shared__ __align__(16) uint8_t smem[];  // x: [chunk][piece 0..7][lane] 16-byte pieces
-  __shared__ __align__(16) uint32_t grid_s[1024];
+  __shared__ uint4 grid_s[256 * 8];  // 8 bank-group copies of the codebook (32 KB)
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int K = p.K;
   const int64_t rb = K / 4, srb = K / 256;  // bytes per weight row, scales per row
@@ -358,7 +361,8 @@ __global__ void __launch_bounds__(kR1Threads, 1) gemv_iq2n_r1_kernel(const R1Par
   const int64_t r1 = static_cast<int64_t>(blockIdx.x + 1) * p.N / gridDim.x;
   const uint16_t* sc = reinterpret_cast<const uint16_t*>(p.sc);
   pdl_trigger();
-  for (int i = tid; i < 1024; i += kR1Threads) grid_s[i] = kIq2xxsGridBf16x2[i];
+  for (int i = tid; i < 256 * 8; i += kR1Threads)
+    grid_s[i] = reinterpret_cast<const uint4*>(kIq2xxsGridBf16x2)[i >> 3];
 
   uint4 wv[RB][KC];
   uint32_t sv[RB][KC];
