@@ -153,7 +153,7 @@ __global__ void __launch_bounds__(kThreads, 2)
     fence_barrier_init();
   }
   if constexpr (FMT == kFmtIq2N) {
-    for (int i = tid; i < 1024; i += kThreads) grid_s[i] = kIq2xxsGridBf16x2[i];
+    load_iq2_grid<false>(grid_s, tid, kThreads);
   }
   __syncthreads();
   pdl_trigger();

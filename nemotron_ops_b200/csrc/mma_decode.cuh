@@ -150,9 +150,24 @@ __device__ __forceinline__ uint32_t iq2_sign_mask(uint32_t pattern, int pair) {
   return (pattern * ((1u << (15 - 2 * pair)) + (1u << (30 - 2 * pair)))) & 0x80008000u;
 }
 
+// The IQ2_XXS codebook in shared memory: plain (256 entries of 16 bytes) or in 8 bank-group copies
+// (entry e of copy c at 16-byte index 8 e + c; lane l reads copy l % 8, so the 8 lanes of a
+// shared-memory phase never share a bank group -- 32 KB).
+template <bool BANKED>
+__device__ __forceinline__ void load_iq2_grid(uint32_t* grid, int tid, int nthreads) {
+  const uint4* src = reinterpret_cast<const uint4*>(kIq2xxsGridBf16x2);
+  uint4* dst = reinterpret_cast<uint4*>(grid);
+  for (int i = tid; i < (BANKED ? 2048 : 256); i += nthreads) dst[i] = src[BANKED ? i >> 3 : i];
+}
+template <bool BANKED>
+__device__ __forceinline__ uint4 iq2_grid_entry(const uint32_t* grid, uint32_t e) {
+  const uint4* g = reinterpret_cast<const uint4*>(grid);
+  return BANKED ? g[8 * e + (threadIdx.x & 7)] : g[e];
+}
+
 // Decodes one row's 16 weights of the chunk into 8 MMA A registers (see the file comment).
-// `grid` points at the 256 x 4 word bf16x2 codebook (shared memory in the kernels).
-template <int FMT>
+// `grid` points at the IQ2_XXS codebook in shared memory (BANKED: the 8-copy layout above).
+template <int FMT, bool BANKED = false>
 __device__ __forceinline__ void decode_row(const RawRow& r, int t, const uint32_t* grid, uint32_t (&out)[8]) {
   if constexpr (FMT == kFmtQ4) {
     const __nv_bfloat162 s2 = bits_bf2(r.s | (r.s << 16));
@@ -198,8 +213,8 @@ __device__ __forceinline__ void decode_row(const RawRow& r, int t, const uint32_
     uint32_t pa = (sg >> (14 * h)) & 127u, pb = (sg >> (14 * h + 7)) & 127u;
     pa |= (__popc(pa) & 1u) << 7;
     pb |= (__popc(pb) & 1u) << 7;
-    const uint4 ga = *reinterpret_cast<const uint4*>(grid + 4 * ia);
-    const uint4 gb = *reinterpret_cast<const uint4*>(grid + 4 * ib);
+    const uint4 ga = iq2_grid_entry<BANKED>(grid, ia);
+    const uint4 gb = iq2_grid_entry<BANKED>(grid, ib);
     const uint32_t gw[8] = {ga.x, ga.y, ga.z, ga.w, gb.x, gb.y, gb.z, gb.w};
 #pragma unroll
     for (int j = 0; j < 8; ++j) {

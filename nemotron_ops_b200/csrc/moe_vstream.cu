@@ -73,7 +73,7 @@ __device__ __forceinline__ uint2 ld_stream8(const void* p) {
 template <int FC, int FMT>
 __global__ void __launch_bounds__(kMsThreads, 1) moe_vstream_kernel(const MsParams p) {
   constexpr bool kIq2n = FMT == kFmtIq2N;
-  __shared__ __align__(16) uint32_t grid_s[kIq2n ? 1024 : 4];  // IQ2_XXS codebook (bf16 pairs)
+  __shared__ __align__(16) uint32_t grid_s[kIq2n ? 8192 : 4];  // IQ2_XXS codebook, 8 bank-group copies
   extern __shared__ __align__(16) uint8_t dsm[];
   __shared__ Groups g;
   __shared__ int tok_pair[kVsMaxSpan][kVsTok];  // fc2: pair of (group slot, token), -1: none
@@ -89,7 +89,7 @@ __global__ void __launch_bounds__(kMsThreads, 1) moe_vstream_kernel(const MsPara
   const int rstride = nch * 16 + 4;  // uint4 per staged source row
 
   if constexpr (kIq2n)
-    for (int i = tid; i < 1024; i += kMsThreads) grid_s[i] = kIq2xxsGridBf16x2[i];
+    load_iq2_grid<true>(grid_s, tid, kMsThreads);
   uint4 zv[4];
   const bool zjob = FC == 1 && tid < p.R * 32;
   if constexpr (FC == 1) {
@@ -263,8 +263,8 @@ __global__ void __launch_bounds__(kMsThreads, 1) moe_vstream_kernel(const MsPara
             decode_q4_mma(h ? w[jj][0].z : w[jj][0].x, h ? w[jj][0].w : w[jj][0].y, s0, a0);
             decode_q4_mma(h ? w[jj][1].z : w[jj][1].x, h ? w[jj][1].w : w[jj][1].y, s1, a1);
           } else if constexpr (kIq2n) {  // half h of the record: its groups 2 h and 2 h + 1
-            decode_row<kFmtIq2N>(RawRow{w[jj][0], s[jj][0]}, h, grid_s, a0);
-            decode_row<kFmtIq2N>(RawRow{w[jj][1], s[jj][1]}, h, grid_s, a1);
+            decode_row<kFmtIq2N, true>(RawRow{w[jj][0], s[jj][0]}, h, grid_s, a0);
+            decode_row<kFmtIq2N, true>(RawRow{w[jj][1], s[jj][1]}, h, grid_s, a1);
           } else {
             decode_row<FMT>(RawRow{make_uint4(h ? w[jj][0].z : w[jj][0].x, h ? w[jj][0].w : w[jj][0].y, 0u, 0u),
                                    s[jj][0]}, 0, nullptr, a0);
@@ -332,7 +332,7 @@ __global__ void __launch_bounds__(kMsThreads, 1) moe_vstream_kernel(const MsPara
   }
 }
 
-std::atomic<size_t> g_vs_smem[3][2] = {{{48 * 1024}, {48 * 1024}}, {{48 * 1024}, {48 * 1024}}, {{48 * 1024}, {48 * 1024}}};
+std::atomic<size_t> g_vs_smem[3][2] = {{{0}, {0}}, {{0}, {0}}, {{0}, {0}}};
 
 template <int FMT>
 cudaError_t launch_layers(const MsParams& p, size_t smem1, size_t smem2, const LaunchCfg& c1, const LaunchCfg& c2) {
