@@ -906,6 +906,12 @@ def main():
             "cpu_baseline": cpu,
             "configs_measured": extra,
         }
+        # the compact per-config numbers go right after the headline keys, the long strings last, so
+        # a reader that keeps only the head of the line still sees every config
+        order = ("metric", "value", "unit", "n_gpus", "steps", "warmup", "ms_per_step", "higher_is_better",
+                 "scaling", "vs_baseline", "dtype", "data", "us_per_call", "configs_measured", "gpu_launches",
+                 "roofline", "clocks", "cpu_baseline", "e2e", "config")
+        line = {k: line[k] for k in order}
         print(json.dumps(line), flush=True)
     if world > 1:
         import torch.distributed as dist
