@@ -135,7 +135,6 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_exact_kernel(const ExactPara
     fence_barrier_init();
   }
   __syncthreads();
-  pdl_trigger();
   if (warp == 0) {
     if (p.early_weights) {
       if (lane == 0) {
@@ -193,6 +192,7 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_exact_kernel(const ExactPara
     }
   }
 
+  pdl_trigger();  // the next call's CTAs start once the activations are loaded, not during our first loads
   for (int i = 0; i < ntiles; ++i) {
     const int s = i % NS;
     const uint32_t ph = (i / NS) & 1;

@@ -156,15 +156,15 @@ __global__ void __launch_bounds__(kThreads, 2)
     load_iq2_grid<false>(grid_s, tid, kThreads);
   }
   __syncthreads();
-  pdl_trigger();
 
   // ------------------------------------------------------------------ producer warp
   if (warp == kCWarps) {
+    int first = 0;
     if (lane == 0) {
       prefetch_tensor_map(&tmw);
       if (p.smode) prefetch_tensor_map(&tms);
       // up-front stages: as many as the ring holds, from the tiles whose scale buffers are free
-      const int first = min(min(NS, nstages), p.nsbuf * KS);
+      first = min(min(NS, nstages), p.nsbuf * KS);
       // weights are constants: with early weights the ring fills, and the rest of the range is
       // pulled into L2, while the previous kernel runs
       const bool rest = nstages > first;
@@ -189,6 +189,14 @@ __global__ void __launch_bounds__(kThreads, 2)
           prefetch_span_l2(p.sc + r0 * sc_row_bytes, static_cast<uint64_t>(nrows) * sc_row_bytes);
         }
       }
+    }
+    // the next call's CTAs are released once the activations have landed (every warp of the CTA
+    // triggers at that point), so their prologues do not compete with this call's first copies
+    __syncwarp();
+    mbar_wait(smem_u32(&x_bar), 0, kStatusFullWait);
+    pdl_trigger();
+    if (lane == 0) {
+      const uint32_t xb = smem_u32(&x_bar);
       int issued = first;
       for (int st = first; st < nstages; ++st) {
         const int s = st % NS;
@@ -266,6 +274,7 @@ __global__ void __launch_bounds__(kThreads, 2)
     }
   }
   named_bar_sync(1, kCWarps * 32);
+  pdl_trigger();  // the activations are converted (see the producer warp)
 
   // ---- per-warp constant offsets (every stage of a tile has the same layout)
   const int wsw = FIX ? 1 : p.wsw;
