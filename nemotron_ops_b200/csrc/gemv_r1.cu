@@ -318,6 +318,97 @@ __global__ void __launch_bounds__(kR1Threads, 1) gemv_q4_r1_kernel(const R1Param
   }
 }
 
+// Q4Gemv int4 at R = 1 with the rows staged through shared memory (the NVFP4 kernel's layout and
+// schedule: one row per warp at a time by cp.async, at most 64 registers, two CTAs per SM, the
+// dependents released once the activations are staged).  Same arithmetic as the register kernel
+// above.  Needs 16-byte aligned scales (the register kernel takes the rest).
+template <int KC>
+__global__ void __launch_bounds__(kR1Threads, 2) gemv_q4_r1s_kernel(const R1Params p) {
+  // [x: PERM pieces [chunk][piece][lane], K * 2 bytes][block sums of x: K / 8 bytes]
+  // [per warp: the row's KC chunks [chunk][lane] 16 B, then its K / 16 bytes of bf16 scales]
+  extern __shared__ __align__(16) uint8_t smem[];
+  constexpr int SLOT = KC * 576;
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int K = p.K;
+  const int64_t rb = K / 2, srb = K / 16;  // bytes per weight row, scale bytes per row
+  const int64_t r0 = static_cast<int64_t>(blockIdx.x) * p.N / gridDim.x;
+  const int64_t r1 = static_cast<int64_t>(blockIdx.x + 1) * p.N / gridDim.x;
+  uint4* xs = reinterpret_cast<uint4*>(smem);
+  float* xsum = reinterpret_cast<float*>(smem + static_cast<size_t>(K) * 2);
+  uint8_t* rowb = smem + static_cast<size_t>(K) * 2 + static_cast<size_t>(K) / 8 + static_cast<size_t>(warp) * SLOT;
+  auto stage_row = [&](int64_t r) {
+    const uint8_t* wr = p.w + r * rb + 16 * lane;
+#pragma unroll
+    for (int i = 0; i < KC; ++i) cp_async16(rowb + i * 512 + 16 * lane, wr + 512 * i);
+    if (lane < KC * 4) cp_async16(rowb + KC * 512 + 16 * lane, p.sc + r * srb + 16 * lane);
+    cp_async_commit();
+  };
+  int64_t r = r0 + warp;
+  if (p.early_weights) {
+    if (r < r1) stage_row(r);
+  } else if (tid == 0) {  // the CTA's rows are contiguous: pull them into L2 during the previous kernel
+    prefetch_span_l2(p.w + r0 * rb, static_cast<uint64_t>(r1 - r0) * rb);
+    prefetch_span_l2(p.sc + r0 * srb, static_cast<uint64_t>(r1 - r0) * srb);
+  }
+  pdl_wait();
+  constexpr int XP = (KC * 128 + kR1Threads - 1) / kR1Threads;  // 16-byte activation pieces per thread
+  uint4 xv[XP];
+#pragma unroll
+  for (int j = 0; j < XP; ++j) {
+    const int q = tid + j * kR1Threads;
+    if (q < K / 8) xv[j] = __ldcg(reinterpret_cast<const uint4*>(p.x) + q);
+  }
+  if (!p.early_weights && r < r1) stage_row(r);
+  // piece q = 4 b + part of scale block b (32 k) = 32 i + l -> PERM pieces [i][part][l], block sums
+#pragma unroll
+  for (int j = 0; j < XP; ++j) {
+    const int q = tid + j * kR1Threads;
+    if (q < K / 8) {  // K / 8 is a multiple of 128: whole warps take this branch
+      const int b = q >> 2, part = q & 3, i = b >> 5, l = b & 31;
+      xs[(i * 4 + part) * 32 + l] = x_piece_to_frag<kFmtQ4>(xv[j]);
+      const uint32_t w4[4] = {xv[j].x, xv[j].y, xv[j].z, xv[j].w};
+      float sum = 0.f;
+#pragma unroll
+      for (int e = 0; e < 4; ++e) sum += __uint_as_float(w4[e] << 16) + __uint_as_float(w4[e] & 0xFFFF0000u);
+      sum += __shfl_xor_sync(0xffffffffu, sum, 1);  // the block's four pieces sit in four adjacent lanes
+      sum += __shfl_xor_sync(0xffffffffu, sum, 2);
+      if (part == 0) xsum[b] = sum;
+    }
+  }
+  __syncthreads();
+  pdl_trigger();  // the next call's CTAs start now, not during this call's activation loads
+
+  for (; r < r1; r += kR1Warps) {
+    cp_async_wait_all();
+    __syncwarp();  // the row's scales were copied by other lanes
+    float acc = 0.f;
+#pragma unroll
+    for (int i = 0; i < KC; ++i) {
+      uint4 x[4];
+#pragma unroll
+      for (int part = 0; part < 4; ++part) x[part] = xs[(i * 4 + part) * 32 + lane];
+      const float xb = xsum[i * 32 + lane];
+      const uint4 wq = lds128(rowb + i * 512 + 16 * lane);
+      const uint32_t sb = *reinterpret_cast<const uint16_t*>(rowb + KC * 512 + 64 * i + 2 * lane);
+      acc = fmaf(fmaf(-136.f, xb, q4_block_dot(wq, x)), bf16_bits_to_f32(sb), acc);
+    }
+    __syncwarp();  // every lane is done with the buffers
+    if (r + kR1Warps < r1) stage_row(r + kR1Warps);  // the warp's next row streams while it reduces
+    const float a = warp_sum(acc);
+    if (lane == 0) p.y[r] = __float2bfloat16(a);
+  }
+  cp_async_wait_all();  // nothing in flight into shared memory at exit
+}
+
+template <int KC>
+cudaError_t launch_q4_r1s(const R1Params& p, int grid, const LaunchCfg& cfg) {
+  const size_t smem = static_cast<size_t>(p.K) * 2 + static_cast<size_t>(p.K) / 8 + static_cast<size_t>(kR1Warps) * KC * 576;
+  auto kern = gemv_q4_r1s_kernel<KC>;
+  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
+  if (e != cudaSuccess) return e;
+  return launch_kernel(kern, dim3(grid), dim3(kR1Threads), smem, cfg, p);
+}
+
 template <int KC>
 cudaError_t launch_q4_r1(const R1Params& p, int grid, const LaunchCfg& cfg) {
   const size_t smem = static_cast<size_t>(p.K) * 2 + static_cast<size_t>(p.K / 32) * 4;
@@ -476,6 +567,18 @@ cudaError_t launch_gemv_r1(int fmt, const bf16* x, const uint8_t* w, const void*
     return cudaErrorNotSupported;
   R1Params p{x, w, static_cast<const uint8_t*>(sc), gscale, y, N, K, cfg.early_weights ? 1 : 0};
   const int grid = static_cast<int>(std::min<int64_t>(cfg.sms, (N + 15) / 16));
+  if (fmt == kFmtQ4 && !(reinterpret_cast<uintptr_t>(sc) & 15)) {
+    switch (K / 1024) {
+      case 1: return launch_q4_r1s<1>(p, grid, cfg);
+      case 2: return launch_q4_r1s<2>(p, grid, cfg);
+      case 3: return launch_q4_r1s<3>(p, grid, cfg);
+      case 4: return launch_q4_r1s<4>(p, grid, cfg);
+      case 5: return launch_q4_r1s<5>(p, grid, cfg);
+      case 6: return launch_q4_r1s<6>(p, grid, cfg);
+      case 7: return launch_q4_r1s<7>(p, grid, cfg);
+      default: return launch_q4_r1s<8>(p, grid, cfg);
+    }
+  }
   if (fmt == kFmtQ4) {
     switch (K / 1024) {
       case 1: return launch_q4_r1<1>(p, grid, cfg);
