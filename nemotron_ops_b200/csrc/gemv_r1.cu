@@ -533,6 +533,98 @@ __global__ void __launch_bounds__(kR1Threads, 1) gemv_iq2n_r1_kernel(const R1Par
   }
 }
 
+// IQ2_XXS at R = 1 with the rows staged through shared memory (the NVFP4 kernel's schedule: one
+// row per warp at a time by cp.async, two CTAs per SM, the dependents released once the
+// activations are staged).  Same arithmetic as the register kernel above.  Needs 16-byte aligned
+// scales (the register kernel takes the rest).  KC = K / 2048.
+template <int KC>
+__global__ void __launch_bounds__(kR1Threads, 2) gemv_iq2n_r1s_kernel(const R1Params p) {
+  // [x: [chunk][piece 0..7][lane] 16-byte pieces, K * 2 bytes][per warp: the row's KC chunks
+  // [chunk][lane] 16 B, then its K / 128 bytes of fp16 superblock scales]
+  extern __shared__ __align__(16) uint8_t smem[];
+  __shared__ uint4 grid_s[256 * 8];  // 8 bank-group copies of the codebook (32 KB)
+  constexpr int SLOT = KC * 528;
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int K = p.K;
+  const int64_t rb = K / 4, srb = K / 128;  // bytes per weight row, scale bytes per row
+  const int64_t r0 = static_cast<int64_t>(blockIdx.x) * p.N / gridDim.x;
+  const int64_t r1 = static_cast<int64_t>(blockIdx.x + 1) * p.N / gridDim.x;
+  for (int i = tid; i < 256 * 8; i += kR1Threads)
+    grid_s[i] = reinterpret_cast<const uint4*>(kIq2xxsGridBf16x2)[i >> 3];
+  uint4* xs = reinterpret_cast<uint4*>(smem);
+  uint8_t* rowb = smem + static_cast<size_t>(K) * 2 + static_cast<size_t>(warp) * SLOT;
+  auto stage_row = [&](int64_t r) {
+    const uint8_t* wr = p.w + r * rb + 16 * lane;
+#pragma unroll
+    for (int i = 0; i < KC; ++i) cp_async16(rowb + i * 512 + 16 * lane, wr + 512 * i);
+    if (lane < KC) cp_async16(rowb + KC * 512 + 16 * lane, p.sc + r * srb + 16 * lane);
+    cp_async_commit();
+  };
+  int64_t r = r0 + warp;
+  if (p.early_weights) {
+    if (r < r1) stage_row(r);
+  } else if (tid == 0) {  // the CTA's rows are contiguous: pull them into L2 during the previous kernel
+    prefetch_span_l2(p.w + r0 * rb, static_cast<uint64_t>(r1 - r0) * rb);
+    prefetch_span_l2(p.sc + r0 * srb, static_cast<uint64_t>(r1 - r0) * srb);
+  }
+  pdl_wait();
+  constexpr int XP = (KC * 256 + kR1Threads - 1) / kR1Threads;  // 16-byte activation pieces per thread
+  uint4 xv[XP];
+#pragma unroll
+  for (int j = 0; j < XP; ++j) {
+    const int q = tid + j * kR1Threads;
+    if (q < K / 8) xv[j] = __ldcg(reinterpret_cast<const uint4*>(p.x) + q);
+  }
+  if (!p.early_weights && r < r1) stage_row(r);
+#pragma unroll
+  for (int j = 0; j < XP; ++j) {  // 8-k piece q -> chunk q / 256, lane (q / 8) % 32, piece q % 8
+    const int q = tid + j * kR1Threads;
+    if (q < K / 8) xs[((q >> 8) * 8 + (q & 7)) * 32 + ((q >> 3) & 31)] = xv[j];
+  }
+  __syncthreads();
+  pdl_trigger();  // the next call's CTAs start now, not during this call's activation loads
+
+  for (; r < r1; r += kR1Warps) {
+    cp_async_wait_all();
+    __syncwarp();  // the row's scales were copied by other lanes
+    float acc = 0.f;
+#pragma unroll
+    for (int i = 0; i < KC; ++i) {
+      const uint4 wq = lds128(rowb + i * 512 + 16 * lane);
+      const uint32_t sb = *reinterpret_cast<const uint16_t*>(rowb + KC * 512 + 16 * i + 2 * (lane >> 2));
+      float a = 0.f, b = 0.f;
+#pragma unroll
+      for (int rec = 0; rec < 2; ++rec) {
+        uint32_t d[16];
+        iq2n_record(rec ? wq.z : wq.x, rec ? wq.w : wq.y, sb, grid_s, d);
+#pragma unroll
+        for (int pc = 0; pc < 4; ++pc) {
+          const uint4 xq = xs[(i * 8 + 4 * rec + pc) * 32 + lane];
+          fma2_bf16_f32r(d[4 * pc], xq.x, a, b);
+          fma2_bf16_f32r(d[4 * pc + 1], xq.y, a, b);
+          fma2_bf16_f32r(d[4 * pc + 2], xq.z, a, b);
+          fma2_bf16_f32r(d[4 * pc + 3], xq.w, a, b);
+        }
+      }
+      acc += a + b;
+    }
+    __syncwarp();  // every lane is done with the buffers
+    if (r + kR1Warps < r1) stage_row(r + kR1Warps);  // the warp's next row streams while it reduces
+    const float v = warp_sum(acc);
+    if (lane == 0) p.y[r] = __float2bfloat16(v);
+  }
+  cp_async_wait_all();  // nothing in flight into shared memory at exit
+}
+
+template <int KC>
+cudaError_t launch_iq2n_r1s(const R1Params& p, int grid, const LaunchCfg& cfg) {
+  const size_t smem = static_cast<size_t>(p.K) * 2 + static_cast<size_t>(kR1Warps) * KC * 528;
+  auto kern = gemv_iq2n_r1s_kernel<KC>;
+  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
+  if (e != cudaSuccess) return e;
+  return launch_kernel(kern, dim3(grid), dim3(kR1Threads), smem, cfg, p);
+}
+
 template <int KC>
 cudaError_t launch_iq2n_r1(const R1Params& p, int grid, const LaunchCfg& cfg) {
   const size_t smem = static_cast<size_t>(p.K) * 2;
@@ -553,6 +645,14 @@ cudaError_t launch_gemv_r1(int fmt, const bf16* x, const uint8_t* w, const void*
       return cudaErrorNotSupported;
     const R1Params q{x, w, static_cast<const uint8_t*>(sc), gscale, y, N, K, cfg.early_weights ? 1 : 0};
     const int grid = static_cast<int>(std::min<int64_t>(cfg.sms, (N + 15) / 16));
+    if (!(reinterpret_cast<uintptr_t>(sc) & 15)) {
+      switch (K / 2048) {
+        case 1: return launch_iq2n_r1s<1>(q, grid, cfg);
+        case 2: return launch_iq2n_r1s<2>(q, grid, cfg);
+        case 3: return launch_iq2n_r1s<3>(q, grid, cfg);
+        default: return launch_iq2n_r1s<4>(q, grid, cfg);
+      }
+    }
     switch (K / 2048) {
       case 1: return launch_iq2n_r1<1>(q, grid, cfg);
       case 2: return launch_iq2n_r1<2>(q, grid, cfg);
