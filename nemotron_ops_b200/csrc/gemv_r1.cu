@@ -21,7 +21,7 @@
 //    After the wait the activations' loads go out first (every CTA reads the same lines, which
 //    return last when queued behind the weight copies), and the dependents are released only
 //    once the activations are staged: 6.64 -> 5.61 us per call at N = 4096, K = 8192.
-// The file also holds the Q4Gemv int4 and IQ2_XXS R = 1 kernels on the same streaming layout (below).
+// The file also holds the Q4Gemv int4 and IQ2_XXS R = 1 kernels on the same layout and schedule (below).
 #include "mma_decode.cuh"
 
 namespace bolt {
@@ -174,11 +174,13 @@ cudaError_t launch_r1(const R1Params& p, int grid, const LaunchCfg& cfg) {
 // ------------------------------------------------------------------------------------------
 // Q4Gemv (int4, zero point 8) at R = 1, exact contract (the reference's R = 1 kernel is
 // QGemvKernel, src/bolt_ops.cu:1315-1392): y = bf16(sum over blocks of s * sum (q - 8) x), fp32.
-// Same streaming layout: lane l reads 16 bytes (one 32-k block) per 1024-k chunk of each row.
-// A warp takes RB rows of its CTA at a time (rows w, w + 16, ...) and shares each activation
-// chunk among them; a lane decodes bf16(128 + q) pairs (a shift and a LOP3 per two weights),
-// multiplies them by x with mixed-precision fma.rn.f32.bf16 (exact products, fp32 sums) and
-// removes 136 * (the block's sum of x); the RB row sums meet in one butterfly reduction.
+// Same layout: lane l takes 16 bytes (one 32-k block) per 1024-k chunk of each row; a lane
+// decodes bf16(128 + q) pairs (a shift and a LOP3 per two weights), multiplies them by x with
+// mixed-precision fma.rn.f32.bf16 (exact products, fp32 sums) and removes 136 * (the block's sum
+// of x).  gemv_q4_r1_kernel (the default) stages a warp's rows through shared memory like the
+// NVFP4 kernel; gemv_q4_r1_reg_kernel, for scales that are not 16-byte aligned, streams RB rows
+// per warp through registers, shares each activation chunk among them and reduces the RB row
+// sums in one butterfly.
 // ------------------------------------------------------------------------------------------
 __device__ __forceinline__ uint32_t ldg_u16(const void* p) {
   unsigned short v;
@@ -240,7 +242,7 @@ __device__ __forceinline__ float warp_sum_t(const float (&v)[RB]) {
 }
 
 template <int KC, int RB>
-__global__ void __launch_bounds__(kR1Threads, 1) gemv_q4_r1_kernel(const R1Params p) {
+__global__ void __launch_bounds__(kR1Threads, 1) gemv_q4_r1_reg_kernel(const R1Params p) {
   extern __shared__ __align__(16) uint8_t smem[];  // x: PERM pieces [chunk][piece][lane], block sums [chunk][lane]
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int K = p.K;
@@ -323,7 +325,7 @@ __global__ void __launch_bounds__(kR1Threads, 1) gemv_q4_r1_kernel(const R1Param
 // dependents released once the activations are staged).  Same arithmetic as the register kernel
 // above.  Needs 16-byte aligned scales (the register kernel takes the rest).
 template <int KC>
-__global__ void __launch_bounds__(kR1Threads, 2) gemv_q4_r1s_kernel(const R1Params p) {
+__global__ void __launch_bounds__(kR1Threads, 2) gemv_q4_r1_kernel(const R1Params p) {
   // [x: PERM pieces [chunk][piece][lane], K * 2 bytes][block sums of x: K / 8 bytes]
   // [per warp: the row's KC chunks [chunk][lane] 16 B, then its K / 16 bytes of bf16 scales]
   extern __shared__ __align__(16) uint8_t smem[];
@@ -401,19 +403,19 @@ __global__ void __launch_bounds__(kR1Threads, 2) gemv_q4_r1s_kernel(const R1Para
 }
 
 template <int KC>
-cudaError_t launch_q4_r1s(const R1Params& p, int grid, const LaunchCfg& cfg) {
+cudaError_t launch_q4_r1(const R1Params& p, int grid, const LaunchCfg& cfg) {
   const size_t smem = static_cast<size_t>(p.K) * 2 + static_cast<size_t>(p.K) / 8 + static_cast<size_t>(kR1Warps) * KC * 576;
-  auto kern = gemv_q4_r1s_kernel<KC>;
+  auto kern = gemv_q4_r1_kernel<KC>;
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
   if (e != cudaSuccess) return e;
   return launch_kernel(kern, dim3(grid), dim3(kR1Threads), smem, cfg, p);
 }
 
 template <int KC>
-cudaError_t launch_q4_r1(const R1Params& p, int grid, const LaunchCfg& cfg) {
+cudaError_t launch_q4_r1_reg(const R1Params& p, int grid, const LaunchCfg& cfg) {
   const size_t smem = static_cast<size_t>(p.K) * 2 + static_cast<size_t>(p.K / 32) * 4;
   constexpr int RB = KC <= 3 ? 4 : 2;  // rows per warp batch: RB * KC <= 12 loads in registers
-  auto kern = gemv_q4_r1_kernel<KC, RB>;
+  auto kern = gemv_q4_r1_reg_kernel<KC, RB>;
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
   if (e != cudaSuccess) return e;
   return launch_kernel(kern, dim3(grid), dim3(kR1Threads), smem, cfg, p);
@@ -423,10 +425,12 @@ cudaError_t launch_q4_r1(const R1Params& p, int grid, const LaunchCfg& cfg) {
 // Q4Gemv iq2 = 2 (native IQ2_XXS records) at R = 1.  Weight contract of the reference's iq2 path:
 // w = +-bf16(mag * bf16(d * (0.5 + s4) * 0.25)) (the decode of mma_decode.cuh), products with x
 // exact and summed in fp32.  A row is K / 4 bytes (an 8-byte record per 32 k); lane l reads 16
-// bytes (two records, 64 k) per 2048-k chunk and the fp16 scale of their 256-k superblock; a warp
-// takes RB rows at a time and shares each activation chunk among them (x in shared memory as
-// [chunk][8-k piece][lane], so a warp's 16-byte reads are contiguous); the codebook sits in shared
-// memory in 8 bank-group copies (conflict-free lookups); the RB row sums meet in one butterfly reduction.
+// bytes (two records, 64 k) per 2048-k chunk and the fp16 scale of their 256-k superblock (x in
+// shared memory as [chunk][8-k piece][lane], so a warp's 16-byte reads are contiguous); the
+// codebook sits in shared memory in 8 bank-group copies (conflict-free lookups).
+// gemv_iq2n_r1_kernel (the default) stages a warp's rows through shared memory like the NVFP4
+// kernel; gemv_iq2n_r1_reg_kernel, for scales that are not 16-byte aligned, streams RB rows per
+// warp through registers and reduces their sums in one butterfly.
 // ------------------------------------------------------------------------------------------
 // One IQ2_XXS record (32 k: four grid indices in idx4; four 7-bit sign patterns and the 4-bit
 // sub-scale in sg) -> 16 bf16 pairs in k order, each +-bf16(mag * bf16(d * (0.5 + s4) * 0.25)):
@@ -451,7 +455,7 @@ __device__ __forceinline__ void iq2n_record(uint32_t idx4, uint32_t sg, uint32_t
 }
 
 template <int KC, int RB>
-__global__ void __launch_bounds__(kR1Threads, 1) gemv_iq2n_r1_kernel(const R1Params p) {
+__global__ void __launch_bounds__(kR1Threads, 1) gemv_iq2n_r1_reg_kernel(const R1Params p) {
   extern __shared__ __align__(16) uint8_t smem[];  // x: [chunk][piece 0..7][lane] 16-byte pieces
   __shared__ uint4 grid_s[256 * 8];  // 8 bank-group copies of the codebook (32 KB)
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
@@ -538,7 +542,7 @@ __global__ void __launch_bounds__(kR1Threads, 1) gemv_iq2n_r1_kernel(const R1Par
 // activations are staged).  Same arithmetic as the register kernel above.  Needs 16-byte aligned
 // scales (the register kernel takes the rest).  KC = K / 2048.
 template <int KC>
-__global__ void __launch_bounds__(kR1Threads, 2) gemv_iq2n_r1s_kernel(const R1Params p) {
+__global__ void __launch_bounds__(kR1Threads, 2) gemv_iq2n_r1_kernel(const R1Params p) {
   // [x: [chunk][piece 0..7][lane] 16-byte pieces, K * 2 bytes][per warp: the row's KC chunks
   // [chunk][lane] 16 B, then its K / 128 bytes of fp16 superblock scales]
   extern __shared__ __align__(16) uint8_t smem[];
@@ -617,19 +621,19 @@ __global__ void __launch_bounds__(kR1Threads, 2) gemv_iq2n_r1s_kernel(const R1Pa
 }
 
 template <int KC>
-cudaError_t launch_iq2n_r1s(const R1Params& p, int grid, const LaunchCfg& cfg) {
+cudaError_t launch_iq2n_r1(const R1Params& p, int grid, const LaunchCfg& cfg) {
   const size_t smem = static_cast<size_t>(p.K) * 2 + static_cast<size_t>(kR1Warps) * KC * 528;
-  auto kern = gemv_iq2n_r1s_kernel<KC>;
+  auto kern = gemv_iq2n_r1_kernel<KC>;
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
   if (e != cudaSuccess) return e;
   return launch_kernel(kern, dim3(grid), dim3(kR1Threads), smem, cfg, p);
 }
 
 template <int KC>
-cudaError_t launch_iq2n_r1(const R1Params& p, int grid, const LaunchCfg& cfg) {
+cudaError_t launch_iq2n_r1_reg(const R1Params& p, int grid, const LaunchCfg& cfg) {
   const size_t smem = static_cast<size_t>(p.K) * 2;
   constexpr int RB = KC <= 1 ? 4 : 2;  // rows per warp batch without spilling
-  auto kern = gemv_iq2n_r1_kernel<KC, RB>;
+  auto kern = gemv_iq2n_r1_reg_kernel<KC, RB>;
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
   if (e != cudaSuccess) return e;
   return launch_kernel(kern, dim3(grid), dim3(kR1Threads), smem, cfg, p);
@@ -647,17 +651,17 @@ cudaError_t launch_gemv_r1(int fmt, const bf16* x, const uint8_t* w, const void*
     const int grid = static_cast<int>(std::min<int64_t>(cfg.sms, (N + 15) / 16));
     if (!(reinterpret_cast<uintptr_t>(sc) & 15)) {
       switch (K / 2048) {
-        case 1: return launch_iq2n_r1s<1>(q, grid, cfg);
-        case 2: return launch_iq2n_r1s<2>(q, grid, cfg);
-        case 3: return launch_iq2n_r1s<3>(q, grid, cfg);
-        default: return launch_iq2n_r1s<4>(q, grid, cfg);
+        case 1: return launch_iq2n_r1<1>(q, grid, cfg);
+        case 2: return launch_iq2n_r1<2>(q, grid, cfg);
+        case 3: return launch_iq2n_r1<3>(q, grid, cfg);
+        default: return launch_iq2n_r1<4>(q, grid, cfg);
       }
     }
     switch (K / 2048) {
-      case 1: return launch_iq2n_r1<1>(q, grid, cfg);
-      case 2: return launch_iq2n_r1<2>(q, grid, cfg);
-      case 3: return launch_iq2n_r1<3>(q, grid, cfg);
-      default: return launch_iq2n_r1<4>(q, grid, cfg);
+      case 1: return launch_iq2n_r1_reg<1>(q, grid, cfg);
+      case 2: return launch_iq2n_r1_reg<2>(q, grid, cfg);
+      case 3: return launch_iq2n_r1_reg<3>(q, grid, cfg);
+      default: return launch_iq2n_r1_reg<4>(q, grid, cfg);
     }
   }
   if ((fmt != kFmtFp4 && fmt != kFmtQ4) || N < 1 || K < 1024 || K % 1024 || K / 1024 > kR1MaxChunks)
@@ -669,18 +673,6 @@ cudaError_t launch_gemv_r1(int fmt, const bf16* x, const uint8_t* w, const void*
   const int grid = static_cast<int>(std::min<int64_t>(cfg.sms, (N + 15) / 16));
   if (fmt == kFmtQ4 && !(reinterpret_cast<uintptr_t>(sc) & 15)) {
     switch (K / 1024) {
-      case 1: return launch_q4_r1s<1>(p, grid, cfg);
-      case 2: return launch_q4_r1s<2>(p, grid, cfg);
-      case 3: return launch_q4_r1s<3>(p, grid, cfg);
-      case 4: return launch_q4_r1s<4>(p, grid, cfg);
-      case 5: return launch_q4_r1s<5>(p, grid, cfg);
-      case 6: return launch_q4_r1s<6>(p, grid, cfg);
-      case 7: return launch_q4_r1s<7>(p, grid, cfg);
-      default: return launch_q4_r1s<8>(p, grid, cfg);
-    }
-  }
-  if (fmt == kFmtQ4) {
-    switch (K / 1024) {
       case 1: return launch_q4_r1<1>(p, grid, cfg);
       case 2: return launch_q4_r1<2>(p, grid, cfg);
       case 3: return launch_q4_r1<3>(p, grid, cfg);
@@ -689,6 +681,18 @@ cudaError_t launch_gemv_r1(int fmt, const bf16* x, const uint8_t* w, const void*
       case 6: return launch_q4_r1<6>(p, grid, cfg);
       case 7: return launch_q4_r1<7>(p, grid, cfg);
       default: return launch_q4_r1<8>(p, grid, cfg);
+    }
+  }
+  if (fmt == kFmtQ4) {
+    switch (K / 1024) {
+      case 1: return launch_q4_r1_reg<1>(p, grid, cfg);
+      case 2: return launch_q4_r1_reg<2>(p, grid, cfg);
+      case 3: return launch_q4_r1_reg<3>(p, grid, cfg);
+      case 4: return launch_q4_r1_reg<4>(p, grid, cfg);
+      case 5: return launch_q4_r1_reg<5>(p, grid, cfg);
+      case 6: return launch_q4_r1_reg<6>(p, grid, cfg);
+      case 7: return launch_q4_r1_reg<7>(p, grid, cfg);
+      default: return launch_q4_r1_reg<8>(p, grid, cfg);
     }
   }
   switch (K / 1024) {
