@@ -108,7 +108,7 @@ def _gemv_workload(kind, R, N, K, iq2=0):
 
         dt = {"nvfp4": "f16", "q8": "f32" if R == 1 else "bf16", "q4": "f32" if (R == 1 and iq2 == 0) else "bf16"}[kind]
         return dict(calls=calls, bytes=nbytes, kernels=1, h2d=R * K * 2, d2h=R * N * 2, e2e=e2e, cpu=cpu,
-                    cpu_sample=N, dtype=dt, kernel="gemv_exact_kernel" if (kind == "q8" and R == 1) else
+                    cpu_sample=N, dtype=dt, kernel="gemv_q8_r1_kernel" if (kind == "q8" and R == 1) else
                     "gemv_nvfp4_r1_kernel" if (kind == "nvfp4" and R == 1) else
                     "gemv_q4_r1_kernel" if (kind == "q4" and R == 1 and iq2 == 0) else
                     "gemv_iq2n_r1_kernel" if (kind == "q4" and R == 1 and iq2 == 2) else "gemv_tc_kernel")

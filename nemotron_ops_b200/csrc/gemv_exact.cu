@@ -357,6 +357,10 @@ bool gemv_exact_stream_ok(int R, int64_t N, int K, const void* x, const void* w,
 
 cudaError_t launch_gemv_exact(int bits, const bf16* x, int R, const uint8_t* w, const bf16* sc, int64_t N, int K,
                               bf16* y, const LaunchCfg& cfg) {
+  if (bits == 8 && R == 1) {  // the staged R = 1 kernel (gemv_r1.cu) where it applies
+    const cudaError_t e = launch_gemv_r1(kFmtQ8, x, w, sc, nullptr, N, K, y, cfg);
+    if (e != cudaErrorNotSupported) return e;
+  }
   if (gemv_exact_stream_ok(R, N, K, x, w, sc)) {
     ExactParams p{x, w, sc, y, N, K, 0, 0, cfg.early_weights ? 1 : 0};
     const uint32_t row_bytes = static_cast<uint32_t>(K) * bits / 8;

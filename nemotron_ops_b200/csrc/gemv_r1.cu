@@ -639,6 +639,111 @@ cudaError_t launch_iq2n_r1_reg(const R1Params& p, int grid, const LaunchCfg& cfg
   return launch_kernel(kern, dim3(grid), dim3(kR1Threads), smem, cfg, p);
 }
 
+// ------------------------------------------------------------------------------------------
+// Q8Gemv at R = 1, exact contract (every weight the exact fp32 (b - 128) * s, fp32 sums; the
+// reference's R = 1 kernel is QGemvKernel, src/bolt_ops.cu:1315-1392), on the NVFP4 kernel's
+// layout and schedule: a warp stages one row at a time through shared memory by cp.async (16
+// bytes = 16 k per lane and 512-k chunk, plus the row's bf16 scales), two CTAs per SM, the
+// dependents released once the activations are staged.  x sits in shared memory as fp32,
+// [chunk][part 0..3][lane] 16 bytes, the 16 k of lane l in k order.  A lane turns four weight
+// bytes into floats with one prmt each (bits 0x4B0000bb = 2^23 + b) and one packed add of
+// -(2^23 + 128) per pair -- exact -- then runs packed fma.rn.f32x2 with x, and scales its 16-k
+// sum once (a 32-k scale block spans two lanes).  KC = K / 512, K <= 4096.
+// ------------------------------------------------------------------------------------------
+template <int KC>
+__global__ void __launch_bounds__(kR1Threads, 2) gemv_q8_r1_kernel(const R1Params p) {
+  extern __shared__ __align__(16) uint8_t smem[];
+  constexpr int SLOT = KC * 544;  // 512 weight bytes + 32 scale bytes per chunk
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int K = p.K;
+  const int64_t rb = K, srb = K / 16;  // bytes per weight row, scale bytes per row
+  const int64_t r0 = static_cast<int64_t>(blockIdx.x) * p.N / gridDim.x;
+  const int64_t r1 = static_cast<int64_t>(blockIdx.x + 1) * p.N / gridDim.x;
+  uint8_t* rowb = smem + static_cast<size_t>(K) * 4 + static_cast<size_t>(warp) * SLOT;
+  auto stage_row = [&](int64_t r) {
+    const uint8_t* wr = p.w + r * rb + 16 * lane;
+#pragma unroll
+    for (int i = 0; i < KC; ++i) cp_async16(rowb + i * 512 + 16 * lane, wr + 512 * i);
+    if (lane < KC * 2) cp_async16(rowb + KC * 512 + 16 * lane, p.sc + r * srb + 16 * lane);
+    cp_async_commit();
+  };
+  int64_t r = r0 + warp;
+  if (p.early_weights) {
+    if (r < r1) stage_row(r);
+  } else if (tid == 0) {  // the CTA's rows are contiguous: pull them into L2 during the previous kernel
+    prefetch_span_l2(p.w + r0 * rb, static_cast<uint64_t>(r1 - r0) * rb);
+    prefetch_span_l2(p.sc + r0 * srb, static_cast<uint64_t>(r1 - r0) * srb);
+  }
+  pdl_wait();
+  constexpr int XP = (KC * 64 + kR1Threads - 1) / kR1Threads;  // 16-byte activation pieces per thread
+  uint4 xv[XP];
+#pragma unroll
+  for (int j = 0; j < XP; ++j) {
+    const int q = tid + j * kR1Threads;
+    if (q < K / 8) xv[j] = __ldcg(reinterpret_cast<const uint4*>(p.x) + q);
+  }
+  if (!p.early_weights && r < r1) stage_row(r);
+  // piece q (8 k) -> chunk q / 64, lane (q % 64) / 2, parts 2 (q % 2) and 2 (q % 2) + 1
+#pragma unroll
+  for (int j = 0; j < XP; ++j) {
+    const int q = tid + j * kR1Threads;
+    if (q < K / 8) {
+      const int i = q >> 6, l = (q & 63) >> 1, h = q & 1;
+      const uint32_t u[4] = {xv[j].x, xv[j].y, xv[j].z, xv[j].w};
+      float f[8];
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        f[2 * e] = __uint_as_float(u[e] << 16);
+        f[2 * e + 1] = __uint_as_float(u[e] & 0xFFFF0000u);
+      }
+      *reinterpret_cast<float4*>(smem + ((i * 4 + 2 * h) * 32 + l) * 16) = make_float4(f[0], f[1], f[2], f[3]);
+      *reinterpret_cast<float4*>(smem + ((i * 4 + 2 * h + 1) * 32 + l) * 16) = make_float4(f[4], f[5], f[6], f[7]);
+    }
+  }
+  __syncthreads();
+  pdl_trigger();  // the next call's CTAs start now, not during this call's activation loads
+
+  const uint32_t M = 0x4B000000u;
+  const float2 zp = make_float2(-8388736.f, -8388736.f);  // -(2^23 + 128)
+  for (; r < r1; r += kR1Warps) {
+    cp_async_wait_all();
+    __syncwarp();  // the row's scales were copied by other lanes
+    float acc = 0.f;
+#pragma unroll
+    for (int i = 0; i < KC; ++i) {
+      const uint4 wq = lds128(rowb + i * 512 + 16 * lane);
+      const uint32_t wd[4] = {wq.x, wq.y, wq.z, wq.w};
+      float2 a = make_float2(0.f, 0.f), b = make_float2(0.f, 0.f);
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        const float4 xq = *reinterpret_cast<const float4*>(smem + ((i * 4 + q) * 32 + lane) * 16);
+        const float2 f01 = fadd2(make_float2(__uint_as_float(prmt(wd[q], M, 0x7440)),
+                                             __uint_as_float(prmt(wd[q], M, 0x7441))), zp);
+        const float2 f23 = fadd2(make_float2(__uint_as_float(prmt(wd[q], M, 0x7442)),
+                                             __uint_as_float(prmt(wd[q], M, 0x7443))), zp);
+        a = ffma2(f01, make_float2(xq.x, xq.y), a);
+        b = ffma2(f23, make_float2(xq.z, xq.w), b);
+      }
+      const uint32_t sb = *reinterpret_cast<const uint16_t*>(rowb + KC * 512 + 32 * i + 2 * (lane >> 1));
+      acc = fmaf((a.x + a.y) + (b.x + b.y), bf16_bits_to_f32(sb), acc);
+    }
+    __syncwarp();  // every lane is done with the buffers
+    if (r + kR1Warps < r1) stage_row(r + kR1Warps);  // the warp's next row streams while it reduces
+    const float v = warp_sum(acc);
+    if (lane == 0) p.y[r] = __float2bfloat16(v);
+  }
+  cp_async_wait_all();  // nothing in flight into shared memory at exit
+}
+
+template <int KC>
+cudaError_t launch_q8_r1(const R1Params& p, int grid, const LaunchCfg& cfg) {
+  const size_t smem = static_cast<size_t>(p.K) * 4 + static_cast<size_t>(kR1Warps) * KC * 544;
+  auto kern = gemv_q8_r1_kernel<KC>;
+  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
+  if (e != cudaSuccess) return e;
+  return launch_kernel(kern, dim3(grid), dim3(kR1Threads), smem, cfg, p);
+}
+
 }  // namespace
 
 cudaError_t launch_gemv_r1(int fmt, const bf16* x, const uint8_t* w, const void* sc, const float* gscale, int64_t N,
@@ -662,6 +767,23 @@ cudaError_t launch_gemv_r1(int fmt, const bf16* x, const uint8_t* w, const void*
       case 2: return launch_iq2n_r1_reg<2>(q, grid, cfg);
       case 3: return launch_iq2n_r1_reg<3>(q, grid, cfg);
       default: return launch_iq2n_r1_reg<4>(q, grid, cfg);
+    }
+  }
+  if (fmt == kFmtQ8) {
+    if (N < 1 || K < 512 || K % 512 || K > 4096 || (reinterpret_cast<uintptr_t>(w) & 15) ||
+        (reinterpret_cast<uintptr_t>(sc) & 15) || (reinterpret_cast<uintptr_t>(x) & 15))
+      return cudaErrorNotSupported;
+    const R1Params q{x, w, static_cast<const uint8_t*>(sc), gscale, y, N, K, cfg.early_weights ? 1 : 0};
+    const int grid = static_cast<int>(std::min<int64_t>(cfg.sms, (N + 15) / 16));
+    switch (K / 512) {
+      case 1: return launch_q8_r1<1>(q, grid, cfg);
+      case 2: return launch_q8_r1<2>(q, grid, cfg);
+      case 3: return launch_q8_r1<3>(q, grid, cfg);
+      case 4: return launch_q8_r1<4>(q, grid, cfg);
+      case 5: return launch_q8_r1<5>(q, grid, cfg);
+      case 6: return launch_q8_r1<6>(q, grid, cfg);
+      case 7: return launch_q8_r1<7>(q, grid, cfg);
+      default: return launch_q8_r1<8>(q, grid, cfg);
     }
   }
   if ((fmt != kFmtFp4 && fmt != kFmtQ4) || N < 1 || K < 1024 || K % 1024 || K / 1024 > kR1MaxChunks)
