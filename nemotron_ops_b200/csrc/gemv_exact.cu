@@ -344,8 +344,9 @@ cudaError_t dispatch_stream(ExactParams& p, int grid, const LaunchCfg& cfg) {
       default: return launch_stream<BITS, 256, 4>(p, grid, cfg);
     }
   }
-  if (nslots >= 128) return launch_stream<BITS, 128, 1>(p, grid, cfg);
-  return launch_stream<BITS, 64, 1>(p, grid, cfg);
+  // every 16-k slot needs a thread: TPR * SPT >= nslots
+  if (nslots >= 128) return nslots > 128 ? launch_stream<BITS, 128, 2>(p, grid, cfg) : launch_stream<BITS, 128, 1>(p, grid, cfg);
+  return nslots > 64 ? launch_stream<BITS, 64, 2>(p, grid, cfg) : launch_stream<BITS, 64, 1>(p, grid, cfg);
 }
 
 }  // namespace
@@ -361,15 +362,17 @@ cudaError_t launch_gemv_exact(int bits, const bf16* x, int R, const uint8_t* w, 
     const cudaError_t e = launch_gemv_r1(kFmtQ8, x, w, sc, nullptr, N, K, y, cfg);
     if (e != cudaErrorNotSupported) return e;
   }
-  if (gemv_exact_stream_ok(R, N, K, x, w, sc)) {
+  const uint32_t budget = cfg.smem_budget ? cfg.smem_budget : 200 * 1024;
+  const uint32_t stage_bytes =
+      (kRowsPerStage * (static_cast<uint32_t>(K) * bits / 8) + kRowsPerStage * (K / 32) * 2 + 32 + 127) & ~127u;
+  // the ring needs two stages in shared memory (Q8 with K > 6016 takes the generic kernel)
+  if (gemv_exact_stream_ok(R, N, K, x, w, sc) && 2 * stage_bytes <= budget) {
     ExactParams p{x, w, sc, y, N, K, 0, 0, cfg.early_weights ? 1 : 0};
-    const uint32_t row_bytes = static_cast<uint32_t>(K) * bits / 8;
-    const uint32_t sc_bytes = kRowsPerStage * (K / 32) * 2 + 32;
-    p.stage_bytes = (kRowsPerStage * row_bytes + sc_bytes + 127) & ~127u;
+    p.stage_bytes = stage_bytes;
     const int grid = static_cast<int>(std::min<int64_t>(cfg.sms, (N + 7) / 8));
     const int64_t rows_per_cta = (N + grid - 1) / grid;
     const int want = static_cast<int>((rows_per_cta + kRowsPerStage - 1) / kRowsPerStage);
-    const int fit = static_cast<int>((cfg.smem_budget ? cfg.smem_budget : 200 * 1024) / p.stage_bytes);
+    const int fit = static_cast<int>(budget / p.stage_bytes);
     p.nstage = std::max(2, std::min({want, fit, 16}));
     return bits == 8 ? dispatch_stream<8>(p, grid, cfg) : dispatch_stream<4>(p, grid, cfg);
   }

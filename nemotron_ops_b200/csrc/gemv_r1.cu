@@ -177,10 +177,8 @@ cudaError_t launch_r1(const R1Params& p, int grid, const LaunchCfg& cfg) {
 // Same layout: lane l takes 16 bytes (one 32-k block) per 1024-k chunk of each row; a lane
 // decodes bf16(128 + q) pairs (a shift and a LOP3 per two weights), multiplies them by x with
 // mixed-precision fma.rn.f32.bf16 (exact products, fp32 sums) and removes 136 * (the block's sum
-// of x).  gemv_q4_r1_kernel (the default) stages a warp's rows through shared memory like the
-// NVFP4 kernel; gemv_q4_r1_reg_kernel, for scales that are not 16-byte aligned, streams RB rows
-// per warp through registers, shares each activation chunk among them and reduces the RB row
-// sums in one butterfly.
+// of x).  gemv_q4_r1_kernel stages a warp's rows through shared memory like the NVFP4 kernel
+// (the C ABI hands it 16-byte aligned tensors only).
 // ------------------------------------------------------------------------------------------
 __device__ __forceinline__ uint32_t ldg_u16(const void* p) {
   unsigned short v;
@@ -241,89 +239,9 @@ __device__ __forceinline__ float warp_sum_t(const float (&v)[RB]) {
   }
 }
 
-template <int KC, int RB>
-__global__ void __launch_bounds__(kR1Threads, 1) gemv_q4_r1_reg_kernel(const R1Params p) {
-  extern __shared__ __align__(16) uint8_t smem[];  // x: PERM pieces [chunk][piece][lane], block sums [chunk][lane]
-  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  const int K = p.K;
-  const int64_t rb = K / 2, srb = K / 32;  // bytes per weight row, scales per row
-  const int64_t r0 = static_cast<int64_t>(blockIdx.x) * p.N / gridDim.x;
-  const int64_t r1 = static_cast<int64_t>(blockIdx.x + 1) * p.N / gridDim.x;
-  const uint16_t* sc = reinterpret_cast<const uint16_t*>(p.sc);
-  pdl_trigger();
-
-  uint4 wv[RB][KC];
-  uint32_t sv[RB][KC];
-  auto load_rows = [&](int64_t ra) {  // rows ra, ra + 16, ... (RB of them, inside the CTA's range)
-#pragma unroll
-    for (int q = 0; q < RB; ++q) {
-      const int64_t r = ra + 16 * q;
-      if (r < r1) {
-        const uint8_t* wr = p.w + r * rb + 16 * lane;
-        const uint16_t* sr = sc + r * srb + lane;
-#pragma unroll
-        for (int i = 0; i < KC; ++i) {
-          wv[q][i] = ldg_stream(wr + 512 * i);
-          sv[q][i] = ldg_u16(sr + 32 * i);
-        }
-      }
-    }
-  };
-  int64_t ra = r0 + warp;
-  if (p.early_weights) {
-    load_rows(ra);
-  } else if (tid == 0) {  // the CTA's rows are contiguous: pull them into L2 during the previous kernel
-    prefetch_span_l2(p.w + r0 * rb, static_cast<uint64_t>(r1 - r0) * rb);
-    prefetch_span_l2(sc + r0 * srb, static_cast<uint64_t>(r1 - r0) * srb * 2);
-  }
-  pdl_wait();
-  if (!p.early_weights) load_rows(ra);
-
-  // activations: block b = 32 i + l of 32 k -> PERM pieces [i][piece][l] and the block's fp32 sum
-  uint4* xs = reinterpret_cast<uint4*>(smem);
-  float* xsum = reinterpret_cast<float*>(smem + static_cast<size_t>(K) * 2);
-  for (int b = tid; b < K / 32; b += kR1Threads) {
-    const uint4* src = reinterpret_cast<const uint4*>(p.x) + 4 * b;
-    const int i = b >> 5, l = b & 31;
-    float sum = 0.f;
-#pragma unroll
-    for (int part = 0; part < 4; ++part) {
-      const uint4 v = __ldcg(src + part);
-      xs[(i * 4 + part) * 32 + l] = x_piece_to_frag<kFmtQ4>(v);
-      const uint32_t w4[4] = {v.x, v.y, v.z, v.w};
-#pragma unroll
-      for (int e = 0; e < 4; ++e) sum += __uint_as_float(w4[e] << 16) + __uint_as_float(w4[e] & 0xFFFF0000u);
-    }
-    xsum[b] = sum;
-  }
-  __syncthreads();
-
-  constexpr int kLanesPerRow = 32 / RB;
-  for (; ra < r1; ra += 16 * RB) {
-    float acc[RB];
-#pragma unroll
-    for (int q = 0; q < RB; ++q) acc[q] = 0.f;
-#pragma unroll
-    for (int i = 0; i < KC; ++i) {
-      uint4 x[4];
-#pragma unroll
-      for (int part = 0; part < 4; ++part) x[part] = xs[(i * 4 + part) * 32 + lane];
-      const float xb = xsum[i * 32 + lane];
-#pragma unroll
-      for (int q = 0; q < RB; ++q)
-        acc[q] = fmaf(fmaf(-136.f, xb, q4_block_dot(wv[q][i], x)), bf16_bits_to_f32(sv[q][i]), acc[q]);
-    }
-    if (ra + 16 * RB < r1) load_rows(ra + 16 * RB);  // the warp's next rows, while it reduces
-    const float v = warp_sum_t<RB>(acc);
-    const int q = lane / kLanesPerRow;
-    if (lane % kLanesPerRow == 0 && ra + 16 * q < r1) p.y[ra + 16 * q] = __float2bfloat16(v);
-  }
-}
-
 // Q4Gemv int4 at R = 1 with the rows staged through shared memory (the NVFP4 kernel's layout and
 // schedule: one row per warp at a time by cp.async, at most 64 registers, two CTAs per SM, the
-// dependents released once the activations are staged).  Same arithmetic as the register kernel
-// above.  Needs 16-byte aligned scales (the register kernel takes the rest).
+// dependents released once the activations are staged).  16-byte aligned scales.
 template <int KC>
 __global__ void __launch_bounds__(kR1Threads, 2) gemv_q4_r1_kernel(const R1Params p) {
   // [x: PERM pieces [chunk][piece][lane], K * 2 bytes][block sums of x: K / 8 bytes]
@@ -411,15 +329,6 @@ cudaError_t launch_q4_r1(const R1Params& p, int grid, const LaunchCfg& cfg) {
   return launch_kernel(kern, dim3(grid), dim3(kR1Threads), smem, cfg, p);
 }
 
-template <int KC>
-cudaError_t launch_q4_r1_reg(const R1Params& p, int grid, const LaunchCfg& cfg) {
-  const size_t smem = static_cast<size_t>(p.K) * 2 + static_cast<size_t>(p.K / 32) * 4;
-  constexpr int RB = KC <= 3 ? 4 : 2;  // rows per warp batch: RB * KC <= 12 loads in registers
-  auto kern = gemv_q4_r1_reg_kernel<KC, RB>;
-  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
-  if (e != cudaSuccess) return e;
-  return launch_kernel(kern, dim3(grid), dim3(kR1Threads), smem, cfg, p);
-}
 
 // ------------------------------------------------------------------------------------------
 // Q4Gemv iq2 = 2 (native IQ2_XXS records) at R = 1.  Weight contract of the reference's iq2 path:
@@ -788,12 +697,12 @@ cudaError_t launch_gemv_r1(int fmt, const bf16* x, const uint8_t* w, const void*
   }
   if ((fmt != kFmtFp4 && fmt != kFmtQ4) || N < 1 || K < 1024 || K % 1024 || K / 1024 > kR1MaxChunks)
     return cudaErrorNotSupported;
-  if ((reinterpret_cast<uintptr_t>(w) & 15) || (reinterpret_cast<uintptr_t>(sc) & (fmt == kFmtQ4 ? 1 : 15)) ||
+  if ((reinterpret_cast<uintptr_t>(w) & 15) || (reinterpret_cast<uintptr_t>(sc) & 15) ||
       (reinterpret_cast<uintptr_t>(x) & 15))
     return cudaErrorNotSupported;
   R1Params p{x, w, static_cast<const uint8_t*>(sc), gscale, y, N, K, cfg.early_weights ? 1 : 0};
   const int grid = static_cast<int>(std::min<int64_t>(cfg.sms, (N + 15) / 16));
-  if (fmt == kFmtQ4 && !(reinterpret_cast<uintptr_t>(sc) & 15)) {
+  if (fmt == kFmtQ4) {
     switch (K / 1024) {
       case 1: return launch_q4_r1<1>(p, grid, cfg);
       case 2: return launch_q4_r1<2>(p, grid, cfg);
@@ -803,18 +712,6 @@ cudaError_t launch_gemv_r1(int fmt, const bf16* x, const uint8_t* w, const void*
       case 6: return launch_q4_r1<6>(p, grid, cfg);
       case 7: return launch_q4_r1<7>(p, grid, cfg);
       default: return launch_q4_r1<8>(p, grid, cfg);
-    }
-  }
-  if (fmt == kFmtQ4) {
-    switch (K / 1024) {
-      case 1: return launch_q4_r1_reg<1>(p, grid, cfg);
-      case 2: return launch_q4_r1_reg<2>(p, grid, cfg);
-      case 3: return launch_q4_r1_reg<3>(p, grid, cfg);
-      case 4: return launch_q4_r1_reg<4>(p, grid, cfg);
-      case 5: return launch_q4_r1_reg<5>(p, grid, cfg);
-      case 6: return launch_q4_r1_reg<6>(p, grid, cfg);
-      case 7: return launch_q4_r1_reg<7>(p, grid, cfg);
-      default: return launch_q4_r1_reg<8>(p, grid, cfg);
     }
   }
   switch (K / 1024) {

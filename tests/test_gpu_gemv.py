@@ -237,6 +237,48 @@ def test_ragged_rows(N, R, fmt):
     assert_contract_close(y, ref)
 
 
+@pytest.mark.parametrize("N,K", [(1000, 2560), (149, 512), (300, 4608), (149, 6144), (149, 8192), (77, 1056),
+                                 (77, 2080)])
+def test_q8_r1_staged_and_exact_paths(N, K):
+    """Q8Gemv R = 1: K % 512 == 0 and K <= 4096 take the shared-memory staged kernel, the other
+    shapes the exact streaming kernel (every 16-k slot count from 65 to 1024) or the generic one;
+    all against the exact contract."""
+    d = W.q8_gemv(R=1, N=N, K=K, seed=K)
+    y = ops.Q8Gemv(d["x"], d["B"], d["scales"])
+    c = _cpu(d)
+    assert_contract_close(y, O.q8_gemv(c["x"], c["B"], c["scales"]))
+
+
+@pytest.mark.parametrize("K", [1056, 2080, 3104])
+def test_q4_r1_exact_stream_slot_counts(K):
+    """Q4Gemv R = 1 with K % 256 != 0: the exact streaming kernel at 66, 130 and 194 slots."""
+    d = W.q4_gemv(R=1, N=77, K=K, seed=K)
+    y = ops.Q4Gemv(d["x"], d["B"], d["scales"])
+    c = _cpu(d)
+    assert_contract_close(y, O.q4_gemv(c["x"], c["B"], c["scales"]))
+
+
+@pytest.mark.parametrize("N,K", [(1000, 2048), (149, 6144), (17, 8192)])
+def test_iq2n_r1_staged_shapes(N, K):
+    """IQ2_XXS R = 1 on the staged kernel at every chunk count it compiles (K / 2048 = 1, 3, 4)."""
+    d = W.q4_gemv(R=1, N=N, K=K, iq2=2, seed=N + K)
+    y = ops.Q4Gemv(d["x"], d["B"], d["scales"], iq2=2)
+    c = _cpu(d)
+    assert_contract_close(y, O.q4_gemv(c["x"], c["B"], c["scales"], iq2=2))
+
+
+def test_iq2n_r1_scales_off_16_bytes_take_register_kernel():
+    """Scales 2 bytes past a 16-byte boundary: the register-streaming IQ2_XXS kernel."""
+    d = W.q4_gemv(R=1, N=300, K=4096, iq2=2, seed=5)
+    s = d["scales"]
+    buf = torch.empty(s.numel() + 1, dtype=s.dtype, device=DEV)
+    s2 = buf[1:].view(s.shape)
+    s2.copy_(s)
+    y = ops.Q4Gemv(d["x"], d["B"], s2, iq2=2)
+    c = _cpu(d)
+    assert_contract_close(y, O.q4_gemv(c["x"], c["B"], c["scales"], iq2=2))
+
+
 @pytest.mark.parametrize("K", [32, 96, 160, 544])
 @pytest.mark.parametrize("R", [1, 4])
 def test_k_not_multiple_of_64(K, R):
