@@ -10,6 +10,7 @@
 #include <cuda_bf16.h>
 #include <cuda_fp16.h>
 #include <cuda_runtime.h>
+#include <atomic>
 #include <stdint.h>
 
 #if defined(__CUDA_ARCH__) && (__CUDA_ARCH__ < 1000)
@@ -150,6 +151,31 @@ __device__ __forceinline__ uint32_t stage_span(uint8_t* dst, const uint8_t* src,
 // and its memory is visible.  A no-op when the kernel was launched without the attribute.
 __device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
 // Lets the next grid in the stream (launched with the PDL attribute) start its prologue.
+// A kernel's dynamic shared-memory limit is raised once per device and size: the attribute call
+// costs host time on every launch otherwise.  One SmemOptIn per kernel (a static beside its
+// launcher; static storage starts at zero).  A kernel with large static shared memory needs the
+// opt-in even for a small dynamic size, which the zero start gives.
+struct SmemOptIn {
+  static constexpr int kMaxDevices = 64;
+  std::atomic<size_t> bytes[kMaxDevices];
+};
+
+template <typename Kern>
+inline cudaError_t allow_smem(Kern kern, size_t bytes, SmemOptIn& s) {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= SmemOptIn::kMaxDevices)
+    return cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(bytes));
+  std::atomic<size_t>& cur = s.bytes[dev];
+  if (bytes <= cur.load(std::memory_order_relaxed)) return cudaSuccess;
+  const cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(bytes));
+  if (e == cudaSuccess) {
+    size_t c = cur.load();
+    while (c < bytes && !cur.compare_exchange_weak(c, bytes)) {
+    }
+  }
+  return e;
+}
+
 __device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;"); }
 
 // Named barrier `id` (1..15) over the first `threads` threads of the block (a multiple of 32);

@@ -327,7 +327,8 @@ template <int BITS, int TPR, int SPT>
 cudaError_t launch_stream(const ExactParams& p, int grid, const LaunchCfg& cfg) {
   auto kern = gemv_exact_kernel<BITS, TPR, SPT>;
   const size_t smem = static_cast<size_t>(p.nstage) * p.stage_bytes;
-  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
+  static SmemOptIn opt;
+  cudaError_t e = allow_smem(kern, smem, opt);
   if (e != cudaSuccess) return e;
   return launch_kernel(kern, dim3(grid), dim3(kThreads), smem, cfg, p);
 }

@@ -492,7 +492,8 @@ template <int FMT, bool BC, int MT, int CPW, bool FIX>
 cudaError_t launch_tc(const CUtensorMap& tmw, const CUtensorMap& tms, const GemvParams& p, int grid, size_t smem,
                       const LaunchCfg& cfg) {
   auto kern = gemv_tc_kernel<FMT, BC, MT, CPW, FIX>;
-  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
+  static SmemOptIn opt;
+  cudaError_t e = allow_smem(kern, smem, opt);
   if (e != cudaSuccess) return e;
   return launch_kernel(kern, dim3(grid), dim3(kThreads), smem, cfg, tmw, tms, p);
 }

@@ -165,7 +165,8 @@ template <int KC>
 cudaError_t launch_r1(const R1Params& p, int grid, const LaunchCfg& cfg) {
   const size_t smem = static_cast<size_t>(p.K) * 2 + static_cast<size_t>(kR1Warps) * (KC * 512 + 512);
   auto kern = gemv_nvfp4_r1_kernel<KC>;
-  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
+  static SmemOptIn opt;
+  cudaError_t e = allow_smem(kern, smem, opt);
   if (e != cudaSuccess) return e;
   return launch_kernel(kern, dim3(grid), dim3(kR1Threads), smem, cfg, p);
 }
@@ -324,7 +325,8 @@ template <int KC>
 cudaError_t launch_q4_r1(const R1Params& p, int grid, const LaunchCfg& cfg) {
   const size_t smem = static_cast<size_t>(p.K) * 2 + static_cast<size_t>(p.K) / 8 + static_cast<size_t>(kR1Warps) * KC * 576;
   auto kern = gemv_q4_r1_kernel<KC>;
-  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
+  static SmemOptIn opt;
+  cudaError_t e = allow_smem(kern, smem, opt);
   if (e != cudaSuccess) return e;
   return launch_kernel(kern, dim3(grid), dim3(kR1Threads), smem, cfg, p);
 }
@@ -533,7 +535,8 @@ template <int KC>
 cudaError_t launch_iq2n_r1(const R1Params& p, int grid, const LaunchCfg& cfg) {
   const size_t smem = static_cast<size_t>(p.K) * 2 + static_cast<size_t>(kR1Warps) * KC * 528;
   auto kern = gemv_iq2n_r1_kernel<KC>;
-  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
+  static SmemOptIn opt;
+  cudaError_t e = allow_smem(kern, smem, opt);
   if (e != cudaSuccess) return e;
   return launch_kernel(kern, dim3(grid), dim3(kR1Threads), smem, cfg, p);
 }
@@ -543,7 +546,8 @@ cudaError_t launch_iq2n_r1_reg(const R1Params& p, int grid, const LaunchCfg& cfg
   const size_t smem = static_cast<size_t>(p.K) * 2;
   constexpr int RB = KC <= 1 ? 4 : 2;  // rows per warp batch without spilling
   auto kern = gemv_iq2n_r1_reg_kernel<KC, RB>;
-  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
+  static SmemOptIn opt;
+  cudaError_t e = allow_smem(kern, smem, opt);
   if (e != cudaSuccess) return e;
   return launch_kernel(kern, dim3(grid), dim3(kR1Threads), smem, cfg, p);
 }
@@ -648,7 +652,8 @@ template <int KC>
 cudaError_t launch_q8_r1(const R1Params& p, int grid, const LaunchCfg& cfg) {
   const size_t smem = static_cast<size_t>(p.K) * 4 + static_cast<size_t>(kR1Warps) * KC * 544;
   auto kern = gemv_q8_r1_kernel<KC>;
-  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
+  static SmemOptIn opt;
+  cudaError_t e = allow_smem(kern, smem, opt);
   if (e != cudaSuccess) return e;
   return launch_kernel(kern, dim3(grid), dim3(kR1Threads), smem, cfg, p);
 }

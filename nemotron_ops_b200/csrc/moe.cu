@@ -643,7 +643,8 @@ template <int FC, int TPR, int SPT>
 cudaError_t launch_seg(const SegParams& p, int grid, const LaunchCfg& cfg) {
   auto kern = moe_seg_kernel<FC, TPR, SPT>;
   const size_t smem = static_cast<size_t>(p.nstage) * p.stage_bytes;
-  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
+  static SmemOptIn opt;
+  cudaError_t e = allow_smem(kern, smem, opt);
   if (e != cudaSuccess) return e;
   return launch_kernel(kern, dim3(grid), dim3(kSegThreads), smem, cfg, p);
 }
@@ -694,8 +695,8 @@ cudaError_t launch_moe_route(const bf16* x, const bf16* gate_w, const float* bia
                       x, gate_w, R, K, E, early, scores);
   } else {
     constexpr size_t smem = 8 * kRoutePassVec * sizeof(uint4);
-    e = cudaFuncSetAttribute(router_logits_kernel<8>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                             static_cast<int>(smem));
+    static SmemOptIn opt;
+    e = allow_smem(router_logits_kernel<8>, smem, opt);
     if (e == cudaSuccess)
       e = launch_kernel(router_logits_kernel<8>, dim3(blocks), dim3(kRouteThreads), smem, cfg, x, gate_w, R, K, E,
                         early, scores);

@@ -338,9 +338,8 @@ __global__ void __launch_bounds__(kMsThreads, 1) moe_stream_fc2_kernel(const MsP
   }
 }
 
-std::atomic<size_t> g_fc1_smem{0};
-std::atomic<size_t> g_fc2_smem[9] = {{0}, {0}, {0}, {0}, {0},
-                                     {0}, {0}, {0}, {0}};
+SmemOptIn g_fc1_smem;
+SmemOptIn g_fc2_smem[9];
 
 template <int F>
 cudaError_t launch_fc2(const MsParams& p, size_t smem, const LaunchCfg& cfg) {

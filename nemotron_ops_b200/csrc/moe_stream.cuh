@@ -160,21 +160,5 @@ __device__ void build_groups(const MsParams& p, Groups& g, bool report) {
   __syncthreads();
 }
 
-
-// raises the kernel's dynamic shared-memory limit to `bytes` when it is below (one attribute call
-// per kernel and size increase; `cur` starts at 0, so the first launch always sets it -- a kernel
-// with large static shared memory needs the opt-in even for a small dynamic size)
-template <typename K>
-cudaError_t allow_smem(K kern, size_t bytes, std::atomic<size_t>& cur) {
-  if (bytes <= cur.load(std::memory_order_relaxed)) return cudaSuccess;
-  const cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(bytes));
-  if (e == cudaSuccess) {
-    size_t c = cur.load();
-    while (c < bytes && !cur.compare_exchange_weak(c, bytes)) {
-    }
-  }
-  return e;
-}
-
 }  // namespace
 }  // namespace bolt

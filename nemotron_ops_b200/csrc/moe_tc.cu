@@ -571,7 +571,8 @@ template <int FMT, bool BC, int CPW, bool FIX, int FC, int WM, int CW, int MT>
 cudaError_t launch_one(const CUtensorMap& tmw, const CUtensorMap& tms, const MoeTcParams& p, size_t smem,
                        const LaunchCfg& cfg) {
   auto kern = moe_tc_kernel<FMT, BC, CPW, FIX, FC, WM, CW, MT>;
-  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
+  static SmemOptIn opt;
+  cudaError_t e = allow_smem(kern, smem, opt);
   if (e != cudaSuccess) return e;
   return launch_kernel(kern, dim3(cfg.sms), dim3((CW + 1) * 32), smem, cfg, tmw, tms, p);
 }

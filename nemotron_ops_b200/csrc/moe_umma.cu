@@ -706,7 +706,8 @@ template <int FMT, int FC>
 cudaError_t launch_umma(const CUtensorMap& tmw, const UmmaParams& p, size_t smem,
                         const LaunchCfg& cfg) {
   auto kern = moe_umma_kernel<FMT, FC>;
-  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
+  static SmemOptIn opt;
+  cudaError_t e = allow_smem(kern, smem, opt);
   if (e != cudaSuccess) return e;
   return launch_kernel(kern, dim3(cfg.sms), dim3(kUThreads), smem, cfg, tmw, p);
 }

@@ -332,11 +332,11 @@ __global__ void __launch_bounds__(kMsThreads, 1) moe_vstream_kernel(const MsPara
   }
 }
 
-std::atomic<size_t> g_vs_smem[3][2] = {{{0}, {0}}, {{0}, {0}}, {{0}, {0}}};
+SmemOptIn g_vs_smem[3][2];
 
 template <int FMT>
 cudaError_t launch_layers(const MsParams& p, size_t smem1, size_t smem2, const LaunchCfg& c1, const LaunchCfg& c2) {
-  std::atomic<size_t>* cur = g_vs_smem[FMT == kFmtQ4 ? 0 : FMT == kFmtIq2N ? 1 : 2];
+  SmemOptIn* cur = g_vs_smem[FMT == kFmtQ4 ? 0 : FMT == kFmtIq2N ? 1 : 2];
   cudaError_t e = allow_smem(moe_vstream_kernel<1, FMT>, smem1, cur[0]);
   if (e != cudaSuccess) return e;
   e = allow_smem(moe_vstream_kernel<2, FMT>, smem2, cur[1]);
