@@ -6,8 +6,8 @@ INFRASTRUCTURE, outputs only under oracle/_ref/ (git-ignored; travels with the t
                            against the stand-in header, linked to nemotron_ops_b200/libbolt_b200.so
   libbolt_ref.so           the reference's own src/bolt_ops.cu compiled from its checkout for
                            sm_100a against the stand-in header -- only where the checkout exists
-                           (BOLT_REFERENCE_DIR, default /root/reference); elsewhere the prebuilt
-                           file is used if present
+                           (BOLT_REFERENCE_DIR, else the build container's read-only checkout);
+                           elsewhere the prebuilt file is used if present
 
     python oracle/ort_shim/build.py [--force]
 """
